@@ -1,0 +1,492 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-linear hot path (one JSON line on rank 0).
+
+Workload (default ``--workload decode``): the INT8
+decode GEMV sweep -- batch M in {1, 4, 8, 16} x (K, N) in {(4096, 12288),
+(12288, 4096), (4096, 151936)}, weights N(0, 0.02) packed to INT8 per output
+channel, activations N(0, 1) quantized to two-pass INT16.  One *step* is the
+12 calls of the sweep.  ``value`` is the whole-job HBM throughput:
+algorithmic bytes of the 12 calls (``N*K*bits/8 + 2*N*K/32 + 4*M*K + 4*M*N``
+each) / device time of the step, max over ranks.  With ``--gpus P`` every layer
+is column-parallel (N/P per GPU) and the output shards are NCCL-all-gathered:
+total work is fixed, so scaling is "strong".
+
+Other BASELINE configs are parity-test cases (tests/), not bench lines.
+
+Inputs stay resident in HBM; every call streams its weights from HBM because
+each small layer is packed into several copies that are rotated (the working
+set of a step, > 1 GB, is far above the 126 MB L2).
+
+``--impl reference`` times the reference's own VNNI/OpenMP ``i4_matmul``
+(oracle/_ref, built from kernel/quantized_matmul.cpp) on the host cores for the
+same sweep and metric; under torchrun only rank 0 runs it.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DECODE_SHAPES = [(4096, 12288), (12288, 4096), (4096, 151936)]   # (K, N)
+DECODE_M = [1, 4, 8, 16]
+PREFILL = dict(K=5120, N=17408, Ms=[128, 512, 2048])
+LAYER = [("q", 5120, 6144), ("k", 5120, 1024), ("v", 5120, 1024), ("o", 6144, 5120),
+         ("gate", 5120, 17408), ("up", 5120, 17408), ("down", 17408, 5120)]
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode GEMV HBM throughput (INT8 weights, two-pass INT16 activations)"
+
+
+def alg_bytes(M, K, N, bits):
+    """Algorithmic bytes of one call (BASELINE.md decode formula, fp16 scales)."""
+    return N * K * bits // 8 + 2 * N * (K // 32) + 4 * M * K + 4 * M * N
+
+
+def decode_kernel_bytes(M, K, N, bits):
+    """Algorithmic bytes of the weight-streaming kernel alone: packed weights,
+    fp16 scales, the two INT8 activation planes and their scales, FP32 output."""
+    return N * K * bits // 8 + 2 * N * (K // 32) + 2 * M * K + 4 * M * (K // 32) + 4 * M * N
+
+
+# ------------------------------------------------------------------ helpers
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the GPU is under load."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ our arm
+
+class Layer:
+    """One packed weight (possibly several rotation copies) of a (K, N) layer shard."""
+
+    def __init__(self, lib, K, N, bits, world, rank, seed, copies):
+        import torch
+        from breeze_engine_b200 import backend
+        from breeze_engine_b200.quant import quantize_matmul_nbits_torch
+        self.K, self.N, self.bits = K, N, bits
+        self.n_local = N // world
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        w = torch.randn((K, N), generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
+        qw, sc, qz = quantize_matmul_nbits_torch(w, bits=bits, per_channel=(bits == 8))
+        del w
+        n0 = rank * self.n_local
+        qw = qw[n0:n0 + self.n_local].contiguous()
+        sc = sc.reshape(N, K // 32)[n0:n0 + self.n_local].contiguous()
+        self.handles = [backend.prepack(qw, sc, None, K, self.n_local, bits) for _ in range(copies)]
+        self.shard_bytes = self.n_local * K * bits // 8 + 2 * self.n_local * (K // 32)
+        del qw, sc
+        torch.cuda.empty_cache()
+
+    def free(self):
+        from breeze_engine_b200 import backend
+        for h in self.handles:
+            backend.free(h)
+
+
+def build_decode(lib, world, rank):
+    import torch
+    layers = []
+    for i, (K, N) in enumerate(DECODE_SHAPES):
+        shard = (N // world) * K + 2 * (N // world) * (K // 32)
+        copies = int(min(len(DECODE_M), max(1, -(-2 * L2_BYTES // shard))))
+        layers.append(Layer(lib, K, N, 8, world, rank, 1000 + i, copies))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    acts = {}
+    for K in sorted({k for k, _ in DECODE_SHAPES}):
+        for M in DECODE_M:
+            acts[(M, K)] = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
+    calls = []
+    for layer in layers:
+        for j, M in enumerate(DECODE_M):
+            calls.append((layer, layer.handles[j % len(layer.handles)], M))
+    return layers, acts, calls
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from breeze_engine_b200 import _lib as L
+    from breeze_engine_b200 import backend
+    from breeze_engine_b200.sharded import gather_columns
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = L.load()
+    backend.set_hi_prec(True)
+    stream = torch.cuda.current_stream()
+    s_ptr = stream.cuda_stream
+
+    layers, acts, calls = build_decode(lib, world, rank)
+    outs, wss = {}, {}
+    for layer, h, M in calls:
+        outs[(id(layer), M)] = torch.empty((M, layer.n_local), dtype=torch.float32, device="cuda")
+        need = lib.ql_workspace_bytes(ctypes.c_void_p(h), M)
+        wss[(layer.K, M)] = torch.empty(max(need, wss.get((layer.K, M), torch.empty(0)).numel()),
+                                        dtype=torch.uint8, device="cuda")
+
+    def step():
+        for layer, h, M in calls:
+            a = acts[(M, layer.K)]
+            c = outs[(id(layer), M)]
+            ws = wss[(layer.K, M)]
+            rc = lib.ql_matmul_dev_ws(ctypes.c_void_p(h), a.data_ptr(), M, c.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), s_ptr)
+            if rc:
+                raise RuntimeError(f"ql_matmul_dev_ws failed: {rc}")
+            if world > 1:
+                gather_columns(c)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            tt = torch.tensor([t], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # keep the GPU busy long enough for the clock sampler to see the timed region
+    t = timed(step, args.steps)
+    clock_info = clocks.stop()
+
+    step_bytes = sum(alg_bytes(M, layer.K, layer.N, layer.bits) for layer, _, M in calls)
+    value = step_bytes * args.steps / t / 1e9
+
+    # ---- per-launch pass for the roofline: the weight-streaming kernel alone
+    kern_t, kern_b, per_call = 0.0, 0, []
+    qws = {}
+    for layer, h, M in calls:
+        key = (M, layer.K)
+        if key not in qws:
+            n = lib.ql_act_workspace_bytes(M, layer.K)
+            qws[key] = torch.empty(n, dtype=torch.uint8, device="cuda")
+            rc = lib.ql_quantize_act_dev(acts[key].data_ptr(), M, layer.K, 1, qws[key].data_ptr(), n, s_ptr)
+            assert rc == 0
+    reps = max(1, args.steps)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
+    times = [0.0] * len(calls)
+    for r in range(reps + 2):
+        for i, (layer, h, M) in enumerate(calls):
+            c = outs[(id(layer), M)]
+            ev[i][0].record(stream)
+            rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), qws[(M, layer.K)].data_ptr(), M, 1,
+                                             c.data_ptr(), s_ptr)
+            ev[i][1].record(stream)
+            assert rc == 0
+        torch.cuda.synchronize()
+        if r >= 2:
+            for i in range(len(calls)):
+                times[i] += ev[i][0].elapsed_time(ev[i][1]) / 1e3
+    for i, (layer, h, M) in enumerate(calls):
+        b = decode_kernel_bytes(M, layer.K, layer.n_local, layer.bits)
+        dt = times[i] / reps
+        kern_t += dt
+        kern_b += b
+        per_call.append({"M": M, "K": layer.K, "N": layer.N, "us": round(dt * 1e6, 2),
+                         "GBps": round(b / dt / 1e9, 1)})
+    peak, peak_kind = measured_peaks()
+    achieved = kern_b / kern_t / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("bytes_per_launch")
+        except Exception:  # noqa: BLE001
+            traffic = None
+
+    # ---- end to end through the reference-compatible host C ABI (i4_matmul)
+    e2e = None
+    if not args.no_e2e:
+        host_a = {k: v.cpu().pin_memory() for k, v in acts.items()}
+        host_c = {k: torch.empty(tuple(v.shape), dtype=torch.float32).pin_memory() for k, v in outs.items()}
+
+        def e2e_step():
+            for layer, h, M in calls:
+                a = host_a[(M, layer.K)]
+                c = host_c[(id(layer), M)]
+                lib.i4_matmul(ctypes.c_void_p(h), ctypes.c_void_p(a.data_ptr()), M, ctypes.c_void_p(c.data_ptr()))
+            return lib.ql_last_status()
+
+        for _ in range(max(1, args.warmup)):
+            assert e2e_step() == 0
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        t_e2e = time.perf_counter() - t0
+        if world > 1:
+            tt = torch.tensor([t_e2e], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t_e2e = float(tt.item())
+        e2e = {"value": round(step_bytes * args.steps / t_e2e / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": int(sum(4 * M * layer.K for layer, _, M in calls)),
+               "d2h_bytes_per_step": int(sum(4 * M * layer.n_local for layer, _, M in calls)),
+               "api": "i4_matmul (host pointers, pinned buffers, synchronous)"
+                      + ("; output stays column-sharded per rank" if world > 1 else "")}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(samples=2)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "s8xs8/u8->s32, f32 rescale", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "configs[1]: INT8 decode GEMV sweep", "M": DECODE_M,
+                       "shapes_KN": DECODE_SHAPES, "weights": "INT8 per-channel RTN, fp16 scales",
+                       "activations": "two-pass INT16 (hi_prec=1)",
+                       "l2": "rotated weight copies; step working set > L2",
+                       "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "kernel": "decode_kernel (ql_gemv.cu)",
+                         "per_call": per_call},
+            "gpu_launches": 2 * len(calls) * args.steps,
+            "clocks": clock_info,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    for layer in layers:
+        layer.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CPU reference
+
+def cpu_has_vnni():
+    try:
+        flags = open("/proc/cpuinfo").read()
+    except OSError:
+        return False
+    return "avx512_vnni" in flags and "avx512vbmi" in flags
+
+
+def host_weights(K, N, bits, seed):
+    """Random MatMulNBits codes + fp16 scales (CPU timing does not depend on values)."""
+    rng = np.random.default_rng(seed)
+    qw = rng.integers(0, 256, (N, K // 32, 4 * bits), dtype=np.uint8)
+    sc = (rng.random(N * (K // 32), dtype=np.float32) * 0.02 + 0.001).astype(np.float16)
+    return qw, sc
+
+
+def _reference_lib():
+    from oracle.oracle import REF_SO, Reference
+    if not os.path.exists(REF_SO):
+        return None, "oracle/_ref/libbreeze_ref.so not built (needs the reference checkout)"
+    if not cpu_has_vnni():
+        return None, "host CPU lacks AVX-512 VNNI/VBMI required by the reference kernel"
+    return Reference(), None
+
+
+def cpu_baseline(samples=2, shapes=None):
+    """Reference i4_matmul (OpenMP, all host threads) over the decode sweep."""
+    os.environ.setdefault("OMP_PROC_BIND", "spread")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref, why = _reference_lib()
+    if ref is None:
+        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": why}
+    threads = os.cpu_count() or 1
+    shapes = shapes or DECODE_SHAPES
+    handles = []
+    for i, (K, N) in enumerate(shapes):
+        qw, sc = host_weights(K, N, 8, 100 + i)
+        handles.append((K, N, ref.prepack(qw, sc, None, K, N, 8)))
+        del qw
+    rng = np.random.default_rng(7)
+    acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32) for K, _ in shapes for M in DECODE_M}
+    outs = {(M, N): np.empty((M, N), np.float32) for _, N in shapes for M in DECODE_M}
+    ref.lib.i4_set_threads(threads)
+    ref.lib.i4_set_hi_prec(1)
+
+    def sweep():
+        for K, N, h in handles:
+            for M in DECODE_M:
+                a, c = acts[(M, K)], outs[(M, N)]
+                ref.lib.i4_matmul(ctypes.c_void_p(h), a.ctypes.data, M, c.ctypes.data)
+
+    sweep()
+    t0 = time.perf_counter()
+    for _ in range(samples):
+        sweep()
+    dt = time.perf_counter() - t0
+    step_bytes = sum(alg_bytes(M, K, N, 8) for K, N, _ in handles for M in DECODE_M)
+    for _, _, h in handles:
+        ref.free(h)
+    return {"value": round(step_bytes * samples / dt / 1e9, 2), "unit": "GB/s", "cores": threads,
+            "kind": "reference", "ms_per_step": round(dt / samples * 1e3, 2),
+            "sample": f"{samples} full decode sweeps (12 i4_matmul calls each) after 1 warm-up, "
+                      f"set_hi_prec(1), OpenMP {threads} threads, OMP_PROC_BIND=spread"}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_PROC_BIND", "spread")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref, why = _reference_lib()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    threads = os.cpu_count() or 1
+    handles = []
+    for i, (K, N) in enumerate(DECODE_SHAPES):
+        qw, sc = host_weights(K, N, 8, 100 + i)
+        handles.append((K, N, ref.prepack(qw, sc, None, K, N, 8)))
+        del qw
+    rng = np.random.default_rng(7)
+    acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32) for K, _ in DECODE_SHAPES for M in DECODE_M}
+    outs = {(M, N): np.empty((M, N), np.float32) for _, N in DECODE_SHAPES for M in DECODE_M}
+    ref.lib.i4_set_threads(threads)
+    ref.lib.i4_set_hi_prec(1)
+
+    def sweep():
+        for K, N, h in handles:
+            for M in DECODE_M:
+                ref.lib.i4_matmul(ctypes.c_void_p(h), acts[(M, K)].ctypes.data, M, outs[(M, N)].ctypes.data)
+
+    for _ in range(args.warmup):
+        sweep()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sweep()
+    dt = time.perf_counter() - t0
+    step_bytes = sum(alg_bytes(M, K, N, 8) for K, N, _ in handles for M in DECODE_M)
+    value = step_bytes * args.steps / dt / 1e9
+    for _, _, h in handles:
+        ref.free(h)
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32 (VPDPBUSD), f32 rescale",
+            "data": "synthetic (random MatMulNBits codes, fp16 scales; N(0,1) activations)",
+            "config": {"workload": "configs[1]: INT8 decode GEMV sweep", "M": DECODE_M,
+                       "shapes_KN": DECODE_SHAPES, "activations": "two-pass INT16 (set_hi_prec(1))",
+                       "parallelism": f"host OpenMP, {threads} threads (rank 0 only)"},
+            "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": f"{args.steps} full sweeps after {args.warmup} warm-ups"},
+            "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

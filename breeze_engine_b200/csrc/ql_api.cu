@@ -1,0 +1,575 @@
+// ql_api.cu -- the C ABI of libbreeze_ql.so (declared in include/breeze_ql.h).
+//
+// Reference-compatible entry points mirror kernel/quantized_matmul.cpp:472-574
+// (i4_set_threads, i4_set_numa_split, i4_set_hi_prec, i4_prepack,
+// i4_prepack_onnx, i4_free, i4_matmul) with the same argument meaning and the
+// same failure behaviour (nullptr handle on a bad contract).  They take host
+// pointers and are synchronous, so an unchanged ctypes or C++ caller works.
+// The ql_* entry points take device pointers and a cudaStream_t (as void*),
+// enqueue asynchronously and return an int status (0 = OK).
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+#include "ql_common.cuh"
+#include "ql_internal.h"
+
+#if defined(__GNUC__)
+#define QL_API extern "C" __attribute__((visibility("default")))
+#else
+#define QL_API extern "C"
+#endif
+
+namespace ql {
+
+__device__ int g_device_error_word = 0;
+
+namespace {
+
+constexpr int MAX_DEVICES = 64;
+
+std::mutex g_mu;
+int g_hi_prec = 0;              // reference default: INT8 single pass (quantized_matmul.cpp:35)
+thread_local int g_last_status = QL_OK;
+thread_local cudaError_t g_last_cuda = cudaSuccess;
+
+struct DeviceState {
+    int* err_word = nullptr;
+    cudaStream_t stream = nullptr;   // for the synchronous host-pointer entry points
+    void* buf = nullptr;             // host-pointer staging: A, C and the activation workspace
+    size_t buf_bytes = 0;
+    void* ws = nullptr;              // workspace for ql_matmul_dev without a caller workspace
+    size_t ws_bytes = 0;
+};
+DeviceState g_dev[MAX_DEVICES];
+
+int set_status(int s, cudaError_t e = cudaSuccess) {
+    g_last_status = s;
+    if (e != cudaSuccess) g_last_cuda = e;
+    return s;
+}
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return set_status(QL_OK);
+    if (e == cudaErrorMemoryAllocation) return set_status(QL_ENOMEM, e);
+    return set_status(QL_ECUDA, e);
+}
+
+// RAII: make `dev` current for the scope of a call, restore afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+DeviceState* state_for(int dev) {
+    if (dev < 0 || dev >= MAX_DEVICES) return nullptr;
+    return &g_dev[dev];
+}
+
+// Grow-only device buffer (caller holds g_mu and has the right device current).
+cudaError_t ensure(void** p, size_t* have, size_t need) {
+    if (*have >= need) return cudaSuccess;
+    if (*p) {
+        cudaFree(*p);   // implicit device synchronisation: no kernel still uses it
+        *p = nullptr;
+        *have = 0;
+    }
+    cudaError_t e = cudaMalloc(p, need);
+    if (e == cudaSuccess) *have = need;
+    return e;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Weight* allocate_weight(int N, int K, int bits, int scale_half, int has_zp) {
+    if (N <= 0 || K <= 0 || N % 16 || K % 32 || (bits != 4 && bits != 8)) return nullptr;
+    auto* w = new (std::nothrow) Weight{};
+    if (!w) return nullptr;
+    w->magic = WEIGHT_MAGIC;
+    w->N = N;
+    w->K = K;
+    w->nblk = K / 32;
+    w->bits = bits;
+    w->scale_half = scale_half;
+    w->has_zp = has_zp;
+    w->G = N / 16;
+    w->nblkZ = (w->nblk + 1) & ~1;
+    cudaGetDevice(&w->device);
+    const size_t tiles = static_cast<size_t>(w->G) * w->nblk;
+    const size_t wb = align256(tiles * (bits == 8 ? 512 : 256));
+    const size_t sb = align256(tiles * 16 * (scale_half ? 2 : 4));
+    const size_t zb = has_zp ? align256(static_cast<size_t>(w->G) * w->nblkZ * 8) : 0;
+    uint8_t* base = nullptr;
+    if (cudaMalloc(&base, wb + sb + zb) != cudaSuccess) {
+        cudaGetLastError();
+        delete w;
+        return nullptr;
+    }
+    w->W = base;
+    w->S = base + wb;
+    w->Z = has_zp ? base + wb + sb : nullptr;
+    w->bytes = wb + sb + zb;
+    return w;
+}
+
+void free_weight(Weight* w) {
+    if (!w) return;
+    w->magic = 0;
+    if (w->W) {
+        DeviceGuard g(w->device);
+        cudaFree(w->W);
+    }
+    delete w;
+}
+
+cudaStream_t internal_stream(DeviceState* st) {
+    if (!st->stream) cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking);
+    return st->stream;
+}
+
+// Workspace for M tokens of K inputs: one activation chunk per 64 tokens,
+// each laid out by act_carve (the quantized planes and scales of that chunk).
+size_t chunk_bytes(int M, int nblk) { return act_bytes(std::min(M, MAX_DECODE_TOKENS), nblk); }
+size_t ws_bytes_for(int M, int nblk) {
+    if (M <= 0) return 0;
+    const size_t chunks = static_cast<size_t>((M + MAX_DECODE_TOKENS - 1) / MAX_DECODE_TOKENS);
+    return chunks * chunk_bytes(M, nblk);
+}
+
+ActView chunk_view(void* ws, int M, int nblk, int c) {
+    const int m0 = c * MAX_DECODE_TOKENS;
+    const int mc = std::min(MAX_DECODE_TOKENS, M - m0);
+    return act_carve(static_cast<uint8_t*>(ws) + static_cast<size_t>(c) * chunk_bytes(M, nblk), mc, nblk);
+}
+
+int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, bool hi_prec) {
+    const int nblk = K / 32;
+    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
+        const ActView act = chunk_view(ws, M, nblk, c);
+        cudaError_t e = launch_quantize_act(dA + static_cast<size_t>(c) * MAX_DECODE_TOKENS * K, K,
+                                            act.M, K, hi_prec, act, stream);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    return set_status(QL_OK);
+}
+
+int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS, cudaStream_t stream,
+                bool hi_prec, bool pdl) {
+    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
+        const ActView act = chunk_view(const_cast<void*>(ws), M, w->nblk, c);
+        const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
+        cudaError_t e = launch_decode(w, act, hi_prec, dC ? dC + m0 * w->N : nullptr, w->N,
+                                      dCS ? dCS + m0 * w->N * w->nblk : nullptr, stream, pdl);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    return set_status(QL_OK);
+}
+
+// Quantize + matmul into a caller workspace of >= ws_bytes_for(M, nblk) bytes.
+// With one chunk the matmul is launched with PDL so it streams weights while
+// the quantizer finishes.
+int run_matmul(const Weight* w, const float* dA, int M, float* dC, int32_t* dCS, void* ws,
+               size_t ws_bytes, cudaStream_t stream, bool hi_prec) {
+    if (ws_bytes < ws_bytes_for(M, w->nblk)) return set_status(QL_EINVAL);
+    if (M <= MAX_DECODE_TOKENS) {
+        int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
+        if (rc != QL_OK) return rc;
+        return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/true);
+    }
+    int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
+    if (rc != QL_OK) return rc;
+    return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/false);
+}
+
+}  // namespace
+
+int* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    DeviceState* st = state_for(dev);
+    if (!st) return nullptr;
+    if (!st->err_word) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        st->err_word = static_cast<int*>(p);
+    }
+    return st->err_word;
+}
+
+}  // namespace ql
+
+using namespace ql;
+
+// ------------------------------------------------------------------ settings
+
+QL_API int ql_version(void) { return 1; }
+
+QL_API int ql_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+// i4_set_threads (kernel/quantized_matmul.cpp:474): accepted for source
+// compatibility; the GPU kernels' results never depend on a thread count.
+QL_API void i4_set_threads(int n) { (void)n; }
+
+// i4_set_numa_split (:475): accepted, no NUMA replica on the GPU.
+QL_API void i4_set_numa_split(int cpu) { (void)cpu; }
+
+// i4_set_hi_prec (:476): process-global activation mode.
+QL_API void i4_set_hi_prec(int on) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_hi_prec = on ? 1 : 0;
+}
+
+QL_API int ql_get_hi_prec(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_hi_prec;
+}
+
+QL_API const char* ql_error_string(int code) {
+    switch (code) {
+        case QL_OK: return "ok";
+        case QL_EINVAL: return "invalid argument";
+        case QL_ENOMEM: return "device allocation failed";
+        case QL_ECUDA: return "CUDA runtime error";
+        case QL_ETIMEOUT: return "bounded device wait timed out";
+        case QL_EDEVICE: return "handle belongs to another device";
+        case QL_ENOTSUP: return "unsupported configuration";
+        default: return "unknown error";
+    }
+}
+
+QL_API int ql_last_status(void) { return g_last_status; }
+
+QL_API const char* ql_last_cuda_error_string(void) { return cudaGetErrorString(g_last_cuda); }
+
+// Reads (and optionally clears) the current device's error word, which kernels
+// set instead of trapping when a bounded wait gives up.  Synchronises the device.
+QL_API int ql_device_error(int clear) {
+    int* w = device_error_word();
+    if (!w) return set_status(QL_ECUDA);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_status(e);
+    int v = 0;
+    e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (clear && v) {
+        const int z = 0;
+        cudaMemcpy(w, &z, sizeof(int), cudaMemcpyHostToDevice);
+    }
+    return v;
+}
+
+// ------------------------------------------------------------------ prepack
+
+// i4_prepack_onnx (kernel/quantized_matmul.cpp:505-520): host MatMulNBits
+// arrays -> owning handle on the current device; nullptr on a bad contract
+// (N,K <= 0, N%16, K%32, bits not 4/8, scale_bits not 16/32, INT8 with
+// qzeros) or allocation failure.  Inputs are deep-copied; the caller may free
+// them as soon as the call returns.
+QL_API void* i4_prepack_onnx(const uint8_t* qw, const void* scales, const uint8_t* qzeros, int N,
+                             int K, int bits, int scale_bits) {
+    if (!qw || !scales || (scale_bits != 16 && scale_bits != 32) || (bits == 8 && qzeros)) {
+        set_status(QL_EINVAL);
+        return nullptr;
+    }
+    Weight* w = allocate_weight(N, K, bits, scale_bits == 16, bits == 4 && qzeros != nullptr);
+    if (!w) {
+        set_status(QL_ENOMEM);
+        return nullptr;
+    }
+    const size_t nblk = w->nblk;
+    const size_t qw_bytes = static_cast<size_t>(N) * nblk * (4 * bits);
+    const size_t sc_bytes = static_cast<size_t>(N) * nblk * (scale_bits / 8);
+    const size_t qz_bytes = w->has_zp ? static_cast<size_t>(N) * ((nblk + 1) / 2) : 0;
+    uint8_t* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, align256(qw_bytes) + align256(sc_bytes) + align256(qz_bytes));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        free_weight(w);
+        set_status(QL_ENOMEM);
+        return nullptr;
+    }
+    uint8_t* d_qw = tmp;
+    uint8_t* d_sc = tmp + align256(qw_bytes);
+    uint8_t* d_qz = d_sc + align256(sc_bytes);
+    cudaStream_t s = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        s = internal_stream(state_for(w->device));
+    }
+    e = cudaMemcpyAsync(d_qw, qw, qw_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_sc, scales, sc_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && qz_bytes) e = cudaMemcpyAsync(d_qz, qzeros, qz_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = launch_prepack_onnx(w, d_qw, d_sc, w->has_zp ? d_qz : nullptr, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        cuda_status(e);
+        free_weight(w);
+        return nullptr;
+    }
+    set_status(QL_OK);
+    return w;
+}
+
+// Device-pointer prepack: the same contract with MatMulNBits arrays already in
+// device memory, enqueued on `stream` (inputs must stay alive until it drains).
+QL_API int ql_prepack_onnx_dev(const uint8_t* d_qw, const void* d_scales, const uint8_t* d_qzeros,
+                               int N, int K, int bits, int scale_bits, void* stream,
+                               void** out_handle) {
+    if (!out_handle) return set_status(QL_EINVAL);
+    *out_handle = nullptr;
+    if (!d_qw || !d_scales || (scale_bits != 16 && scale_bits != 32) || (bits == 8 && d_qzeros))
+        return set_status(QL_EINVAL);
+    if (N <= 0 || K <= 0 || N % 16 || K % 32 || (bits != 4 && bits != 8)) return set_status(QL_EINVAL);
+    Weight* w = allocate_weight(N, K, bits, scale_bits == 16, bits == 4 && d_qzeros != nullptr);
+    if (!w) return set_status(QL_ENOMEM);
+    cudaError_t e = launch_prepack_onnx(w, d_qw, d_scales, w->has_zp ? d_qzeros : nullptr,
+                                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_status(e);
+    }
+    *out_handle = w;
+    return set_status(QL_OK);
+}
+
+// i4_prepack (kernel/quantized_matmul.cpp:480-499): legacy entry taking the
+// reference's already-transformed VNNI layout (srcB [N/16][nblk][8][32|64],
+// srcScale fp32 [N/16][nblk][16], srcZp int8 [N/16][nblk][16] for INT4,
+// srcCorr int32, which this library recomputes implicitly and ignores).
+// INT4 zero points must lie in 0..15 (the MatMulNBits range).
+QL_API void* i4_prepack(const uint8_t* srcB, const float* srcScale, const int8_t* srcZp,
+                        const int32_t* srcCorr, int N, int K, int nblk, int bits) {
+    if (!srcB || !srcScale || !srcCorr || (bits == 4 && !srcZp) || nblk != K / 32 || N <= 0 ||
+        K <= 0 || N % 16 || K % 32) {
+        set_status(QL_EINVAL);
+        return nullptr;
+    }
+    const size_t metas = static_cast<size_t>(N) * nblk;
+    if (bits == 4) {
+        for (size_t i = 0; i < metas; ++i)
+            if (srcZp[i] < 0 || srcZp[i] > 15) {
+                set_status(QL_EINVAL);
+                return nullptr;
+            }
+    }
+    Weight* w = allocate_weight(N, K, bits, 0, bits == 4);
+    if (!w) {
+        set_status(QL_ENOMEM);
+        return nullptr;
+    }
+    const size_t b_bytes = metas * (bits == 8 ? 32 : 16);
+    const size_t s_bytes = metas * 4;
+    const size_t z_bytes = bits == 4 ? metas : 0;
+    uint8_t* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, align256(b_bytes) + align256(s_bytes) + align256(z_bytes));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        free_weight(w);
+        set_status(QL_ENOMEM);
+        return nullptr;
+    }
+    uint8_t* d_b = tmp;
+    float* d_s = reinterpret_cast<float*>(tmp + align256(b_bytes));
+    int8_t* d_z = reinterpret_cast<int8_t*>(tmp + align256(b_bytes) + align256(s_bytes));
+    cudaStream_t s = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        s = internal_stream(state_for(w->device));
+    }
+    e = cudaMemcpyAsync(d_b, srcB, b_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_s, srcScale, s_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && z_bytes) e = cudaMemcpyAsync(d_z, srcZp, z_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = launch_prepack_vnni(w, d_b, d_s, bits == 4 ? d_z : nullptr, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        cuda_status(e);
+        free_weight(w);
+        return nullptr;
+    }
+    set_status(QL_OK);
+    return w;
+}
+
+// i4_free (:522-524): null-safe.
+QL_API void i4_free(void* handle) {
+    if (!valid_weight(handle)) return;
+    free_weight(static_cast<Weight*>(handle));
+}
+
+QL_API int ql_weight_info(const void* handle, int* N, int* K, int* bits, int* device,
+                          unsigned long long* bytes) {
+    if (!valid_weight(handle)) return set_status(QL_EINVAL);
+    const auto* w = static_cast<const Weight*>(handle);
+    if (N) *N = w->N;
+    if (K) *K = w->K;
+    if (bits) *bits = w->bits;
+    if (device) *device = w->device;
+    if (bytes) *bytes = w->bytes;
+    return set_status(QL_OK);
+}
+
+// ------------------------------------------------------------------ matmul
+
+// Workspace bytes ql_matmul_dev_ws needs for M rows (0 for M <= 0).
+QL_API size_t ql_workspace_bytes(const void* handle, int M) {
+    if (!valid_weight(handle) || M <= 0) return 0;
+    const auto* w = static_cast<const Weight*>(handle);
+    return ws_bytes_for(M, w->nblk);
+}
+
+static int check_call(const void* handle, const float* dA, int M, const void* dOut) {
+    if (!valid_weight(handle) || M < 0) return QL_EINVAL;
+    if (M == 0) return QL_OK;
+    if (!dA || !dOut) return QL_EINVAL;
+    if (reinterpret_cast<uintptr_t>(dA) % 16) return QL_EINVAL;     // 16-byte vector loads
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return QL_ECUDA;
+    if (dev != static_cast<const Weight*>(handle)->device) return QL_EDEVICE;
+    return QL_OK;
+}
+
+// C[M,N] = matmul(A[M,K]) with a caller workspace of >= ql_workspace_bytes().
+// The handle's device must be current.  Asynchronous on `stream`.
+QL_API int ql_matmul_dev_ws(void* handle, const float* dA, int M, float* dC, void* ws,
+                            size_t ws_bytes, void* stream) {
+    const int c = check_call(handle, dA, M, dC);
+    if (c != QL_OK || M == 0) return set_status(c);
+    if (!ws) return set_status(QL_EINVAL);
+    return run_matmul(static_cast<Weight*>(handle), dA, M, dC, nullptr, ws, ws_bytes,
+                      static_cast<cudaStream_t>(stream), ql_get_hi_prec() != 0);
+}
+
+// Same, with the library's per-device workspace.  Calls that share a device
+// are serialised on the host; the workspace is reused in stream order.
+QL_API int ql_matmul_dev(void* handle, const float* dA, int M, float* dC, void* stream) {
+    const int c = check_call(handle, dA, M, dC);
+    if (c != QL_OK || M == 0) return set_status(c);
+    const auto* w = static_cast<const Weight*>(handle);
+    const bool hp = ql_get_hi_prec() != 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* st = state_for(w->device);
+    const size_t need = ws_bytes_for(M, w->nblk);
+    cudaError_t e = ensure(&st->ws, &st->ws_bytes, need);
+    if (e != cudaSuccess) return cuda_status(e);
+    return run_matmul(w, dA, M, dC, nullptr, st->ws, st->ws_bytes, static_cast<cudaStream_t>(stream), hp);
+}
+
+// Scratch bytes for M quantized activation rows of width K (0 for M <= 0).
+QL_API size_t ql_act_workspace_bytes(int M, int K) {
+    if (M <= 0 || K <= 0 || K % 32) return 0;
+    return ws_bytes_for(M, K / 32);
+}
+
+// Quantize activations once into `ws` (the kernels' layout) so several
+// weights that share the input (Q/K/V, gate/up) reuse them.
+QL_API int ql_quantize_act_dev(const float* dA, int M, int K, int hi_prec, void* ws, size_t ws_bytes,
+                               void* stream) {
+    if (M < 0 || K <= 0 || K % 32) return set_status(QL_EINVAL);
+    if (M == 0) return set_status(QL_OK);
+    if (!dA || !ws || reinterpret_cast<uintptr_t>(dA) % 16 || ws_bytes < ws_bytes_for(M, K / 32))
+        return set_status(QL_EINVAL);
+    return run_quantize(dA, M, K, ws, static_cast<cudaStream_t>(stream), hi_prec != 0);
+}
+
+// C[M,N] from activations quantized by ql_quantize_act_dev with the same M, K
+// and hi_prec.  Streams the packed weights once per 64-token chunk.
+QL_API int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, float* dC,
+                                   void* stream) {
+    if (!valid_weight(handle) || M < 0) return set_status(QL_EINVAL);
+    if (M == 0) return set_status(QL_OK);
+    if (!ws || !dC) return set_status(QL_EINVAL);
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return set_status(QL_ECUDA);
+    const auto* w = static_cast<const Weight*>(handle);
+    if (dev != w->device) return set_status(QL_EDEVICE);
+    return run_compute(w, ws, M, dC, nullptr, static_cast<cudaStream_t>(stream), hi_prec != 0, false);
+}
+
+// Per-block INT32 accumulators cs[M][N][K/32] = sum_k q16 * (w - zp), produced
+// by the decode kernel's own integer MMA path (parity checks of the INT32 stage).
+QL_API int ql_block_sums_dev(void* handle, const float* dA, int M, int32_t* dCS, void* stream) {
+    const int c = check_call(handle, dA, M, dCS);
+    if (c != QL_OK || M == 0) return set_status(c);
+    const auto* w = static_cast<const Weight*>(handle);
+    const bool hp = ql_get_hi_prec() != 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* st = state_for(w->device);
+    cudaError_t e = ensure(&st->ws, &st->ws_bytes, ws_bytes_for(M, w->nblk));
+    if (e != cudaSuccess) return cuda_status(e);
+    return run_matmul(w, dA, M, nullptr, dCS, st->ws, st->ws_bytes, static_cast<cudaStream_t>(stream), hp);
+}
+
+// The activation quantizer in the reference's layout: hi/lo u8 [M][K] and
+// ascale fp32 [M][K/32] (quantize_A_i16, kernel/quantized_matmul.cpp:237-258).
+QL_API int ql_quantize_dev(const float* dA, int M, int K, uint8_t* dHi, uint8_t* dLo,
+                           float* dAscale, void* stream) {
+    if (M < 0 || K <= 0 || K % 32) return set_status(QL_EINVAL);
+    if (M == 0) return set_status(QL_OK);
+    if (!dA || !dHi || !dLo || !dAscale) return set_status(QL_EINVAL);
+    return cuda_status(launch_quantize_ref(dA, M, K, dHi, dLo, dAscale, static_cast<cudaStream_t>(stream)));
+}
+
+// i4_matmul (kernel/quantized_matmul.cpp:526-552): host A[M,K] fp32 in, host
+// C[M,N] fp32 out, synchronous.  Like the reference it returns nothing; a
+// failure leaves C untouched and is reported by ql_last_status().
+QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
+    if (!valid_weight(handle) || M < 0 || (M > 0 && (!A || !C))) {
+        set_status(QL_EINVAL);
+        return;
+    }
+    if (M == 0) {
+        set_status(QL_OK);
+        return;
+    }
+    const auto* w = static_cast<const Weight*>(handle);
+    const bool hp = ql_get_hi_prec() != 0;
+    DeviceGuard guard(w->device);
+    if (!guard.ok) {
+        set_status(QL_ECUDA);
+        return;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* st = state_for(w->device);
+    cudaStream_t s = internal_stream(st);
+    const size_t a_bytes = align256(static_cast<size_t>(M) * w->K * 4);
+    const size_t c_bytes = align256(static_cast<size_t>(M) * w->N * 4);
+    const size_t ws_bytes = ws_bytes_for(M, w->nblk);
+    cudaError_t e = ensure(&st->buf, &st->buf_bytes, a_bytes + c_bytes + ws_bytes);
+    if (e != cudaSuccess) {
+        cuda_status(e);
+        return;
+    }
+    float* dA = static_cast<float*>(st->buf);
+    float* dC = reinterpret_cast<float*>(static_cast<uint8_t*>(st->buf) + a_bytes);
+    void* ws = static_cast<uint8_t*>(st->buf) + a_bytes + c_bytes;
+    e = cudaMemcpyAsync(dA, A, static_cast<size_t>(M) * w->K * 4, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        cuda_status(e);
+        return;
+    }
+    int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
+    if (rc != QL_OK) return;
+    e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cuda_status(e);
+}

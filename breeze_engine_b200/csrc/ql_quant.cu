@@ -1,0 +1,180 @@
+// ql_quant.cu -- activation quantizer (FP32 -> per-32-block INT16 hi/lo planes).
+//
+// Bit-exact restatement on the GPU of the reference quantize_A_i16
+// (kernel/quantized_matmul.cpp:237-258) and, for the single-pass mode,
+// quantize_A (:215-232):
+//   amax  = max |a| over the block (a NaN never wins the compare)
+//   scale = amax / 32767.f            (__fdiv_rn: IEEE division, one rounding)
+//   inv   = scale > 0 ? 1.f / scale : 0
+//   q     = clamp((int)lrint(a * inv), -32767, 32767)
+// lrint rounds to nearest-even and the reference truncates its 64-bit result
+// to int: NaN / inf / |x| >= 2^63 give 0, |x| in [2^31, 2^63) keep the low
+// 32 bits.  to_int_like_lrint() reproduces that for every float.
+//
+// One thread owns one (token, block) pair: it reads 128 contiguous bytes of A
+// and writes 16-byte chunks of each plane, so the kernel is a single HBM pass.
+#include "ql_common.cuh"
+#include "ql_internal.h"
+
+namespace ql {
+
+__device__ __forceinline__ int to_int_like_lrint(float x) {
+    const float ax = fabsf(x);
+    if (ax < 2147483648.0f) return __float2int_rn(x);
+    if (ax < 9.2233720368547758e18f) return static_cast<int>(static_cast<uint32_t>(
+                                                static_cast<unsigned long long>(__float2ll_rn(x))));
+    return 0;   // NaN, +-inf, |x| >= 2^63
+}
+
+template <bool HP>
+__global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ A, int lda,
+                                                           int M, int K, ActView out) {
+    // Let a dependent (PDL) kernel start its weight streaming right away; it
+    // still waits for this grid's completion before reading the planes.
+    pdl_launch_dependents();
+    const int nblk = K / BLOCK_K;
+    const int Mpad = out.MT * 8;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(Mpad) * nblk) return;
+    const int m = static_cast<int>(idx / nblk);
+    const int b = static_cast<int>(idx % nblk);
+
+    // [b][m/8][khalf][m%8][16]
+    const size_t grp = (static_cast<size_t>(b) * out.MT + (m >> 3)) * 256 + (m & 7) * 16;
+    uint4* hs0 = reinterpret_cast<uint4*>(out.hs + grp);
+    uint4* hs1 = reinterpret_cast<uint4*>(out.hs + grp + 128);
+    uint4* lo0 = reinterpret_cast<uint4*>(out.lo + grp);
+    uint4* lo1 = reinterpret_cast<uint4*>(out.lo + grp + 128);
+
+    if (m >= M) {   // padded token rows
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        if (HP) { *hs0 = z; *hs1 = z; }
+        *lo0 = z; *lo1 = z;
+        out.as[static_cast<size_t>(b) * Mpad + m] = 0.0f;
+        return;
+    }
+
+    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = __ldg(src + i);
+        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float a = fabsf(v[i]);
+        amax = (a > amax) ? a : amax;
+    }
+    constexpr float QMAX = HP ? 32767.0f : 127.0f;
+    constexpr int IMAX = HP ? 32767 : 127;
+    const float scale = __fdiv_rn(amax, QMAX);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    out.as[static_cast<size_t>(b) * Mpad + m] = scale;
+
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t hword = 0, lword = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int q = to_int_like_lrint(__fmul_rn(v[4 * w + j], inv));
+            q = q > IMAX ? IMAX : (q < -IMAX ? -IMAX : q);
+            if (HP) {
+                const uint32_t u = static_cast<uint32_t>(q + 32768);
+                hword |= ((u >> 8) ^ 0x80u) << (8 * j);      // hi - 128 as a signed byte
+                lword |= (u & 0xFFu) << (8 * j);
+            } else {
+                lword |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);   // q8 as a signed byte
+            }
+        }
+        hw[w] = hword;
+        lw[w] = lword;
+    }
+    if (HP) {
+        *hs0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *hs1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    }
+    *lo0 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *lo1 = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+}
+
+// Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
+// reference's au8_hi / au8_lo) and ascale [M][K/32].
+__global__ void __launch_bounds__(256) quantize_ref_kernel(const float* __restrict__ A, int M, int K,
+                                                           uint8_t* __restrict__ hi,
+                                                           uint8_t* __restrict__ lo,
+                                                           float* __restrict__ ascale) {
+    const int nblk = K / BLOCK_K;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(M) * nblk) return;
+    const int m = static_cast<int>(idx / nblk);
+    const int b = static_cast<int>(idx % nblk);
+    const float* a = A + static_cast<size_t>(m) * K + b * BLOCK_K;
+    float amax = 0.0f;
+    for (int i = 0; i < 32; ++i) {
+        const float v = fabsf(a[i]);
+        amax = (v > amax) ? v : amax;
+    }
+    const float scale = __fdiv_rn(amax, 32767.0f);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    ascale[idx] = scale;
+    for (int i = 0; i < 32; ++i) {
+        int q = to_int_like_lrint(__fmul_rn(a[i], inv));
+        q = q > 32767 ? 32767 : (q < -32767 ? -32767 : q);
+        const uint32_t u = static_cast<uint32_t>(q + 32768);
+        hi[static_cast<size_t>(m) * K + b * BLOCK_K + i] = static_cast<uint8_t>(u >> 8);
+        lo[static_cast<size_t>(m) * K + b * BLOCK_K + i] = static_cast<uint8_t>(u & 0xFF);
+    }
+}
+
+// Token groups of 8, rounded up to a power of two (the decode kernel is
+// instantiated for 1, 2, 4 and 8 groups; padded tokens are zero rows).
+static int act_groups(int M) {
+    const int mt = (M + 7) / 8;
+    return mt <= 1 ? 1 : mt <= 2 ? 2 : mt <= 4 ? 4 : 8;
+}
+
+size_t act_bytes(int M, int nblk) {
+    const size_t MT = static_cast<size_t>(act_groups(M));
+    const size_t plane = (static_cast<size_t>(nblk) * MT * 256 + 255) & ~size_t(255);
+    const size_t as = (static_cast<size_t>(nblk) * MT * 8 * 4 + 255) & ~size_t(255);
+    return 2 * plane + as;
+}
+
+ActView act_carve(void* ws, int M, int nblk) {
+    ActView v;
+    v.M = M;
+    v.MT = act_groups(M);
+    v.nblk = nblk;
+    const size_t plane = (static_cast<size_t>(nblk) * v.MT * 256 + 255) & ~size_t(255);
+    v.hs = static_cast<uint8_t*>(ws);
+    v.lo = v.hs + plane;
+    v.as = reinterpret_cast<float*>(v.lo + plane);
+    return v;
+}
+
+cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
+                                const ActView& out, cudaStream_t stream) {
+    const long long total = static_cast<long long>(out.MT) * 8 * (K / BLOCK_K);
+    const int threads = 256;
+    const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+    if (hi_prec)
+        quantize_act_kernel<true><<<grid, threads, 0, stream>>>(A, lda, M, K, out);
+    else
+        quantize_act_kernel<false><<<grid, threads, 0, stream>>>(A, lda, M, K, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,
+                                float* ascale, cudaStream_t stream) {
+    const long long total = static_cast<long long>(M) * (K / BLOCK_K);
+    if (total == 0) return cudaSuccess;
+    const int threads = 256;
+    const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+    quantize_ref_kernel<<<grid, threads, 0, stream>>>(A, M, K, hi, lo, ascale);
+    return cudaGetLastError();
+}
+
+}  // namespace ql

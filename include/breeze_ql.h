@@ -1,0 +1,153 @@
+/*
+ * breeze_ql.h -- C ABI of libbreeze_ql.so, the sm_100a (B200) quantized-linear
+ * library that replaces Breeze's AVX-512 VNNI kernel (kernel/quantized_matmul.cpp).
+ *
+ * Two groups of entry points:
+ *
+ *  1. Reference-compatible (host pointers, synchronous), same names, argument
+ *     meaning and failure behaviour as kernel/quantized_matmul.cpp:472-574, so
+ *     the unchanged ctypes bridge (breeze/cpu_backend.py:14-54) or the native
+ *     decoders that link i4_matmul (kernel/qwen35_decoder.cpp:124) can bind them.
+ *     Handles own device memory on the device current at prepack time.
+ *
+ *  2. Device-pointer entry points (ql_*): inputs/outputs in device memory,
+ *     cudaStream_t passed as void*, asynchronous, int status (0 = QL_OK).
+ *     The handle's device must be the current device.
+ *
+ * Numerics (both groups, two-pass mode): activations are quantized per 32-wide
+ * K block to INT16 exactly as quantize_A_i16 (kernel/quantized_matmul.cpp:237-258);
+ * per-block INT32 accumulators sum_k q16*(w-zp) are exact; the FP32 rescale
+ * acc = fma(ascale, (float)cs * bscale, acc) runs in ascending block order, so
+ * outputs are bit-identical to i4_matmul on the same inputs.
+ */
+#ifndef BREEZE_QL_H
+#define BREEZE_QL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes of the ql_* entry points. */
+enum {
+    QL_OK = 0,
+    QL_EINVAL = 1,    /* bad argument or contract violation            */
+    QL_ENOMEM = 2,    /* device allocation failed                      */
+    QL_ECUDA = 3,     /* CUDA runtime error (see ql_last_cuda_error_string) */
+    QL_ETIMEOUT = 4,  /* a bounded device wait gave up                 */
+    QL_EDEVICE = 5,   /* handle belongs to another device              */
+    QL_ENOTSUP = 6    /* unsupported configuration                     */
+};
+
+/* ---------------------------------------------------------------- group 1 */
+
+/* Replaces i4_set_threads (kernel/quantized_matmul.cpp:474).  Accepted and
+ * ignored: GPU results do not depend on a thread count. */
+void i4_set_threads(int n);
+
+/* Replaces i4_set_numa_split (kernel/quantized_matmul.cpp:475).  Accepted and
+ * ignored: there is no NUMA weight replica on the GPU. */
+void i4_set_numa_split(int cpu);
+
+/* Replaces i4_set_hi_prec (kernel/quantized_matmul.cpp:476).  Process-global:
+ * 1 = two-pass INT16 activations, 0 = single-pass INT8 (the default, as in the
+ * reference).  Serialise with running calls. */
+void i4_set_hi_prec(int on);
+
+/* Replaces i4_prepack_onnx (kernel/quantized_matmul.cpp:505-520).  qw: uint8
+ * MatMulNBits weights [N][K/32][16] (bits 4) or [N][K/32][32] (bits 8);
+ * scales: [N][K/32] fp16 (scale_bits 16) or fp32 (32); qzeros: packed INT4
+ * zero points [N][ceil(K/64)] or NULL (zp 8; must be NULL for bits 8).
+ * Returns an owning handle on the current device, or NULL on a bad contract
+ * (N,K <= 0, N%16, K%32, bits not 4/8, scale_bits not 16/32, INT8 with
+ * qzeros) or allocation failure.  Inputs may be freed after the call. */
+void* i4_prepack_onnx(const uint8_t* qw, const void* scales, const uint8_t* qzeros, int N, int K,
+                      int bits, int scale_bits);
+
+/* Replaces i4_prepack (kernel/quantized_matmul.cpp:480-499), the legacy entry
+ * taking the reference's VNNI layout: srcB [N/16][nblk][8][32 or 64],
+ * srcScale fp32 [N/16][nblk][16], srcZp int8 [N/16][nblk][16] (INT4, values
+ * 0..15), srcCorr int32 [N/16][nblk][16] (required, not used).  NULL on a bad
+ * contract or allocation failure. */
+void* i4_prepack(const uint8_t* srcB, const float* srcScale, const int8_t* srcZp,
+                 const int32_t* srcCorr, int N, int K, int nblk, int bits);
+
+/* Replaces i4_free (kernel/quantized_matmul.cpp:522-524).  NULL-safe. */
+void i4_free(void* handle);
+
+/* Replaces i4_matmul (kernel/quantized_matmul.cpp:526-552): C[M,N] =
+ * A[M,K] @ dequant(W).T with host fp32 row-major A and C, synchronous.  Like
+ * the reference it returns nothing; a failure leaves C untouched and sets
+ * ql_last_status(). */
+void i4_matmul(void* handle, const float* A, int M, float* C);
+
+/* ---------------------------------------------------------------- group 2 */
+
+/* Library ABI version (no counterpart in the reference). */
+int ql_version(void);
+
+/* Number of visible CUDA devices (0 when none or the driver is absent);
+ * backs available() of the Python bridge (breeze/cpu_backend.py:57). */
+int ql_device_count(void);
+
+/* Current activation mode (the value last given to i4_set_hi_prec). */
+int ql_get_hi_prec(void);
+
+/* Status of this thread's last call, and its description. */
+int ql_last_status(void);
+const char* ql_error_string(int code);
+const char* ql_last_cuda_error_string(void);
+
+/* Synchronises the current device and returns its device error word (set by
+ * a kernel whose bounded wait gave up; 0 = none).  clear != 0 resets it. */
+int ql_device_error(int clear);
+
+/* Device-pointer twin of i4_prepack_onnx: the same contract with the
+ * MatMulNBits arrays already in device memory, enqueued on `stream`. */
+int ql_prepack_onnx_dev(const uint8_t* d_qw, const void* d_scales, const uint8_t* d_qzeros, int N,
+                        int K, int bits, int scale_bits, void* stream, void** out_handle);
+
+/* Handle metadata (any pointer may be NULL). */
+int ql_weight_info(const void* handle, int* N, int* K, int* bits, int* device,
+                   unsigned long long* bytes);
+
+/* Scratch bytes ql_matmul_dev_ws needs for M rows (quantized activations). */
+size_t ql_workspace_bytes(const void* handle, int M);
+
+/* Device twin of i4_matmul (kernel/quantized_matmul.cpp:528): dA [M,K] fp32
+ * (16-byte aligned), dC [M,N] fp32, asynchronous on `stream`, with the
+ * caller's workspace of at least ql_workspace_bytes(handle, M) bytes. */
+int ql_matmul_dev_ws(void* handle, const float* dA, int M, float* dC, void* ws, size_t ws_bytes,
+                     void* stream);
+
+/* Same with the library's per-device workspace (allocated on first use). */
+int ql_matmul_dev(void* handle, const float* dA, int M, float* dC, void* stream);
+
+/* Split form of ql_matmul_dev_ws (no counterpart in the reference, whose
+ * i4_matmul re-quantizes per call, kernel/quantized_matmul.cpp:532-536):
+ * quantize dA [M,K] once into `ws` (>= ql_act_workspace_bytes(M, K) bytes),
+ * then run any number of weights with the same K over it.  hi_prec selects
+ * the activation mode explicitly and must match between the two calls. */
+size_t ql_act_workspace_bytes(int M, int K);
+int ql_quantize_act_dev(const float* dA, int M, int K, int hi_prec, void* ws, size_t ws_bytes,
+                        void* stream);
+int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, float* dC,
+                            void* stream);
+
+/* The per-block INT32 accumulators cs[M][N][K/32] = sum_k q16*(w-zp) of the
+ * reference's tile_kernel (kernel/quantized_matmul.cpp:298-312, 262-268),
+ * produced by this library's own integer MMA path (INT32 parity checks). */
+int ql_block_sums_dev(void* handle, const float* dA, int M, int32_t* dCS, void* stream);
+
+/* The activation quantizer in the reference's layout: dHi/dLo u8 [M][K] and
+ * dAscale fp32 [M][K/32] (quantize_A_i16, kernel/quantized_matmul.cpp:237-258). */
+int ql_quantize_dev(const float* dA, int M, int K, uint8_t* dHi, uint8_t* dLo, float* dAscale,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BREEZE_QL_H */

@@ -1,0 +1,146 @@
+"""Golden-vector cases for the quantized-linear hot path.
+
+Each case builds MatMulNBits inputs and FP32 activations deterministically.
+``make_golden.py`` runs the compiled reference (``kernel/quantized_matmul.cpp``
+via ``oracle/_ref``) on them and stores its outputs in ``golden.npz``; the
+tests rebuild the inputs, check them against the stored SHA-256, and compare
+the oracle and the CUDA library with the stored reference outputs.
+
+Input recipes follow the reference's own tests:
+  * ``pack_*``    -- ``tests/test_cpu_packing.py:33-96`` (fixture_weights:
+    seed N+K+bits, edge bytes [0,1,7,15,127,128,254,255], uniform scales,
+    explicit or default zero points; activations default_rng(5), rows 1 and 9,
+    both activation modes).
+  * ``width_*``   -- ``tests/test_qwen35_cpu.py:196-208`` (27B projection widths,
+    default_rng(3), M=3, two-pass mode).
+  * ``subnormal`` -- ``tests/test_cpu_packing.py:114-131`` (fp16 subnormal and
+    signed-zero scales).
+  * ``edge``      -- activations with zero, subnormal, huge, NaN/inf and
+    outlier blocks (quantizer corner cases).
+  * ``rtn_*``     -- this package's RTN packer on N(0, 0.02) weights with the
+    BASELINE distributions (N(0,1) activations, 1% of channels x20), small sizes.
+"""
+import hashlib
+
+import numpy as np
+
+EDGE_BYTES = [0, 1, 7, 15, 127, 128, 254, 255]
+
+
+def fixture_weights(N, K, bits, dtype, explicit_zeros):
+    rng = np.random.default_rng(N + K + bits)
+    blocks = K // 32
+    qw = rng.integers(0, 256, (N, blocks, 4 * bits), dtype=np.uint8)
+    qw.reshape(-1)[:8] = EDGE_BYTES
+    scales = rng.uniform(0.0001, 0.02, (N, blocks)).astype(dtype)
+    zeros = None
+    if explicit_zeros:
+        zeros = (rng.integers(0, 256, (N, (blocks + 1) // 2), dtype=np.uint8)
+                 if bits == 4 else np.full((N, blocks), 128, np.uint8))
+    return qw, scales, zeros
+
+
+def _pack_case(N, K, bits, dtype, zeros):
+    qw, sc, qz = fixture_weights(N, K, bits, dtype, zeros)
+    rng = np.random.default_rng(5)
+    acts = []
+    for hp in (False, True):
+        for rows in (1, 9):
+            acts.append((hp, rng.normal(size=(rows, K)).astype(np.float32)))
+    return dict(N=N, K=K, bits=bits, qweight=qw, scales=sc, qzeros=qz, acts=acts)
+
+
+def _width_case(K, N, bits):
+    rng = np.random.default_rng(3)
+    qw = rng.integers(0, 256, (N, K // 32, 32 * bits // 8), dtype=np.uint8)
+    sc = rng.uniform(0.001, 0.005, (N, K // 32)).astype(np.float32)
+    a = rng.normal(size=(3, K)).astype(np.float32)
+    return dict(N=N, K=K, bits=bits, qweight=qw, scales=sc, qzeros=None,
+                acts=[(True, a), (False, a)])
+
+
+def _subnormal_case():
+    qw, _, _ = fixture_weights(16, 32, 4, np.float16, False)
+    sc = np.array([0, 0x8000, 1, 0x8001, 0x03FF, 0x0400, 0x3C00, 0x7BFF] * 2,
+                  dtype=np.uint16).view(np.float16).reshape(16, 1)
+    rng = np.random.default_rng(5)
+    acts = [(hp, rng.normal(size=(rows, 32)).astype(np.float32)) for hp in (False, True) for rows in (1, 9)]
+    return dict(N=16, K=32, bits=4, qweight=qw, scales=sc, qzeros=None, acts=acts)
+
+
+def edge_activations(M, K, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.normal(size=(M, K)).astype(np.float32)
+    a[0, 0:32] = 0.0                                            # zero block: scale 0
+    a[0, 32:64] = np.float32(1e-40)                             # subnormal block: inv = inf
+    a[0, 64:96] = np.float32(3e38)                              # huge block
+    a[0, 96:128] = np.float32(1e-36) * np.arange(32, dtype=np.float32)   # tiny ramp
+    if M > 1:
+        a[1, 5] = np.nan
+        a[1, 40] = np.inf
+        a[1, 70] = -np.inf
+    if M > 2:
+        a[2, 128:160] = -7.25                                   # constant block (all +-32767)
+        a[2, 160:192] = np.float32(2.0) ** -126                 # smallest normal
+    a[:, -1] *= 20.0                                            # outlier channel
+    return a
+
+
+def _edge_case(bits, zeros, dtype):
+    N, K = 32, 256
+    qw, sc, qz = fixture_weights(N, K, bits, dtype, zeros)
+    a = edge_activations(5, K, 11)
+    return dict(N=N, K=K, bits=bits, qweight=qw, scales=sc, qzeros=qz, acts=[(True, a), (False, a)])
+
+
+def outlier_activations(M, K, seed, frac=0.01, factor=20.0):
+    """N(0,1) activations with ``frac`` of the channels scaled by ``factor``."""
+    rng = np.random.default_rng(seed)
+    a = rng.normal(size=(M, K)).astype(np.float32)
+    n_out = max(1, int(round(frac * K)))
+    cols = rng.choice(K, size=n_out, replace=False)
+    a[:, cols] *= np.float32(factor)
+    return a
+
+
+def _rtn_case(N, K, bits, M, symmetric, per_channel, outliers, seed):
+    from breeze_engine_b200.quant import quantize_matmul_nbits
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0.0, 0.02, size=(K, N)).astype(np.float32)
+    qw, sc, qz = quantize_matmul_nbits(w, bits=bits, symmetric=symmetric, per_channel=per_channel)
+    a = outlier_activations(M, K, seed + 1) if outliers else \
+        np.random.default_rng(seed + 1).normal(size=(M, K)).astype(np.float32)
+    return dict(N=N, K=K, bits=bits, qweight=qw, scales=sc, qzeros=qz, acts=[(True, a)])
+
+
+def all_cases():
+    cases = {}
+    for (N, K) in [(16, 32), (48, 96), (64, 512)]:
+        for bits in (4, 8):
+            for dtype in (np.float16, np.float32):
+                for zeros in (False, True):
+                    name = f"pack_{N}x{K}_b{bits}_{np.dtype(dtype).name}_{'zp' if zeros else 'nozp'}"
+                    cases[name] = lambda N=N, K=K, bits=bits, dtype=dtype, zeros=zeros: \
+                        _pack_case(N, K, bits, dtype, zeros)
+    for (K, N, bits) in [(5120, 48, 8), (17408, 16, 4), (6144, 64, 8), (4096, 32, 4)]:
+        cases[f"width_{K}x{N}_b{bits}"] = lambda K=K, N=N, bits=bits: _width_case(K, N, bits)
+    cases["subnormal"] = _subnormal_case
+    cases["edge_b4_zp"] = lambda: _edge_case(4, True, np.float16)
+    cases["edge_b4_nozp"] = lambda: _edge_case(4, False, np.float32)
+    cases["edge_b8"] = lambda: _edge_case(8, False, np.float16)
+    cases["rtn_b4_m1"] = lambda: _rtn_case(64, 4096, 4, 1, True, False, False, 101)
+    cases["rtn_b4_outliers"] = lambda: _rtn_case(32, 512, 4, 17, True, False, True, 103)
+    cases["rtn_b4_asym"] = lambda: _rtn_case(48, 1024, 4, 5, False, False, True, 105)
+    cases["rtn_b8_perchannel"] = lambda: _rtn_case(48, 1024, 8, 16, True, True, False, 107)
+    return cases
+
+
+def input_digest(case):
+    h = hashlib.sha256()
+    for key in ("qweight", "scales", "qzeros"):
+        v = case[key]
+        h.update(b"-" if v is None else np.ascontiguousarray(v).tobytes())
+    for hp, a in case["acts"]:
+        h.update(bytes([hp]))
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()

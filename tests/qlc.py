@@ -1,0 +1,98 @@
+"""Test helpers that drive libbreeze_ql.so through its C ABI (include/breeze_ql.h).
+
+Device memory comes from torch (plumbing only); every compute call goes
+through the library's exported ``extern "C"`` entry points via ctypes.
+"""
+import ctypes
+
+import numpy as np
+
+from breeze_engine_b200 import _lib as L
+
+_vp = ctypes.c_void_p
+
+
+def lib():
+    return L.load()
+
+
+def prepack(qweight, scales, qzeros, N, K, bits):
+    """i4_prepack_onnx with host arrays (the reference-compatible entry)."""
+    qw = np.ascontiguousarray(qweight, np.uint8)
+    s = np.asarray(scales)
+    sc = np.ascontiguousarray(s if s.dtype == np.float16 else s.astype(np.float32))
+    qz = None
+    if qzeros is not None and bits == 4:
+        qz = np.ascontiguousarray(qzeros, np.uint8)
+    h = lib().i4_prepack_onnx(qw.ctypes.data, sc.ctypes.data, qz.ctypes.data if qz is not None else None,
+                              N, K, bits, sc.itemsize * 8)
+    assert h, f"i4_prepack_onnx failed: status {lib().ql_last_status()}"
+    return h
+
+
+def free(h):
+    lib().i4_free(_vp(h))
+
+
+def set_hi_prec(on):
+    lib().i4_set_hi_prec(1 if on else 0)
+
+
+def matmul_host(h, a, N):
+    """i4_matmul: host pointers, synchronous."""
+    a = np.ascontiguousarray(a, np.float32)
+    c = np.full((a.shape[0], N), np.float32(-12345.0))
+    lib().i4_matmul(_vp(h), a.ctypes.data, a.shape[0], c.ctypes.data)
+    assert lib().ql_last_status() == 0, lib().ql_error_string(lib().ql_last_status())
+    return c
+
+
+def matmul_dev(h, a, N, workspace=True):
+    """ql_matmul_dev_ws (or ql_matmul_dev) on torch device buffers."""
+    import torch
+    a = np.ascontiguousarray(a, np.float32)
+    M = a.shape[0]
+    dA = torch.from_numpy(a).cuda()
+    dC = torch.full((M, N), -12345.0, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    if workspace:
+        need = lib().ql_workspace_bytes(_vp(h), M)
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+        rc = lib().ql_matmul_dev_ws(_vp(h), dA.data_ptr(), M, dC.data_ptr(), ws.data_ptr(), need, stream)
+    else:
+        rc = lib().ql_matmul_dev(_vp(h), dA.data_ptr(), M, dC.data_ptr(), stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return dC.cpu().numpy()
+
+
+def block_sums_dev(h, a, N, K):
+    import torch
+    a = np.ascontiguousarray(a, np.float32)
+    M = a.shape[0]
+    dA = torch.from_numpy(a).cuda()
+    dCS = torch.full((M, N, K // 32), -7, dtype=torch.int32, device="cuda")
+    rc = lib().ql_block_sums_dev(_vp(h), dA.data_ptr(), M, dCS.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return dCS.cpu().numpy()
+
+
+def quantize_dev(a):
+    import torch
+    a = np.ascontiguousarray(a, np.float32)
+    M, K = a.shape
+    dA = torch.from_numpy(a).cuda()
+    hi = torch.empty((M, K), dtype=torch.uint8, device="cuda")
+    lo = torch.empty((M, K), dtype=torch.uint8, device="cuda")
+    asc = torch.empty((M, K // 32), dtype=torch.float32, device="cuda")
+    rc = lib().ql_quantize_dev(dA.data_ptr(), M, K, hi.data_ptr(), lo.data_ptr(), asc.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return hi.cpu().numpy(), lo.cpu().numpy(), asc.cpu().numpy()
+
+
+def device_error(clear=True):
+    return lib().ql_device_error(1 if clear else 0)
