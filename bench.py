@@ -189,22 +189,19 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local_rank))
     lib = L.load()
     backend.set_hi_prec(True)
-    stream = torch.cuda.current_stream()
-    s_ptr = stream.cuda_stream
 
     layers, acts, calls = build_decode(lib, world, rank)
     outs, wss = {}, {}
     for layer, h, M in calls:
         outs[(id(layer), M)] = torch.empty((M, layer.n_local), dtype=torch.float32, device="cuda")
         need = lib.ql_workspace_bytes(ctypes.c_void_p(h), M)
-        wss[(layer.K, M)] = torch.empty(max(need, wss.get((layer.K, M), torch.empty(0)).numel()),
-                                        dtype=torch.uint8, device="cuda")
+        if (layer.K, M) not in wss or wss[(layer.K, M)].numel() < need:
+            wss[(layer.K, M)] = torch.empty(need, dtype=torch.uint8, device="cuda")
 
     def step():
+        s_ptr = torch.cuda.current_stream().cuda_stream
         for layer, h, M in calls:
-            a = acts[(M, layer.K)]
-            c = outs[(id(layer), M)]
-            ws = wss[(layer.K, M)]
+            a, c, ws = acts[(M, layer.K)], outs[(id(layer), M)], wss[(layer.K, M)]
             rc = lib.ql_matmul_dev_ws(ctypes.c_void_p(h), a.data_ptr(), M, c.data_ptr(),
                                       ws.data_ptr(), ws.numel(), s_ptr)
             if rc:
@@ -216,67 +213,87 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    def timed(fn, steps):
-        barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        t = e0.elapsed_time(e1) / 1e3
+    def max_over_ranks(t):
         if world > 1:
             tt = torch.tensor([t], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             t = float(tt.item())
         return t
 
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    for _ in range(args.warmup):
+    # Eager warm-up (function attributes, NCCL communicators), then one CUDA
+    # graph per step so host submission latency never shows in device time.
+    for _ in range(2):
         step()
     torch.cuda.synchronize()
-    # keep the GPU busy long enough for the clock sampler to see the timed region
-    t = timed(step, args.steps)
+    barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+
+    def timed_replays(g, n):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / 1e3)
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    # Clock window: keep the same load running ~1 s while nvidia-smi samples,
+    # then take the timed region right after it.
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t_probe = timed_replays(graph, 5) / 5
+    n_window = max(1, int(1.0 / max(t_probe, 1e-6)))
+    timed_replays(graph, n_window)
+    t = timed_replays(graph, args.steps)
     clock_info = clocks.stop()
+    clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
 
     step_bytes = sum(alg_bytes(M, layer.K, layer.N, layer.bits) for layer, _, M in calls)
     value = step_bytes * args.steps / t / 1e9
 
-    # ---- per-launch pass for the roofline: the weight-streaming kernel alone
-    kern_t, kern_b, per_call = 0.0, 0, []
+    # ---- per-launch pass (roofline): the weight-streaming kernel alone, on
+    # activations quantized once, REPS launches per call rotating over the
+    # layer's weight copies, captured in a graph and timed with CUDA events.
     qws = {}
     for layer, h, M in calls:
         key = (M, layer.K)
         if key not in qws:
             n = lib.ql_act_workspace_bytes(M, layer.K)
             qws[key] = torch.empty(n, dtype=torch.uint8, device="cuda")
-            rc = lib.ql_quantize_act_dev(acts[key].data_ptr(), M, layer.K, 1, qws[key].data_ptr(), n, s_ptr)
+            rc = lib.ql_quantize_act_dev(acts[key].data_ptr(), M, layer.K, 1, qws[key].data_ptr(), n,
+                                         stream.cuda_stream)
             assert rc == 0
-    reps = max(1, args.steps)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
-    times = [0.0] * len(calls)
-    for r in range(reps + 2):
-        for i, (layer, h, M) in enumerate(calls):
-            c = outs[(id(layer), M)]
-            ev[i][0].record(stream)
-            rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), qws[(M, layer.K)].data_ptr(), M, 1,
-                                             c.data_ptr(), s_ptr)
-            ev[i][1].record(stream)
-            assert rc == 0
-        torch.cuda.synchronize()
-        if r >= 2:
-            for i in range(len(calls)):
-                times[i] += ev[i][0].elapsed_time(ev[i][1]) / 1e3
-    for i, (layer, h, M) in enumerate(calls):
+    torch.cuda.synchronize()
+    REPS = 8
+    kern_t, kern_b, per_call = 0.0, 0, []
+    for layer, h0, M in calls:
+        c, ws = outs[(id(layer), M)], qws[(M, layer.K)]
+        gk = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gk):
+            s_ptr = torch.cuda.current_stream().cuda_stream
+            for r in range(REPS):
+                h = layer.handles[(layer.handles.index(h0) + r) % len(layer.handles)]
+                rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s_ptr)
+                assert rc == 0
+        gk.replay()
+        dt = timed_replays(gk, max(2, args.steps // 2)) / (max(2, args.steps // 2) * REPS)
         b = decode_kernel_bytes(M, layer.K, layer.n_local, layer.bits)
-        dt = times[i] / reps
         kern_t += dt
         kern_b += b
         per_call.append({"M": M, "K": layer.K, "N": layer.N, "us": round(dt * 1e6, 2),
                          "GBps": round(b / dt / 1e9, 1)})
+        del gk
     peak, peak_kind = measured_peaks()
     achieved = kern_b / kern_t / 1e9
     traffic = None
@@ -306,11 +323,7 @@ def run_ours(args):
         t0 = time.perf_counter()
         for _ in range(args.steps):
             e2e_step()
-        t_e2e = time.perf_counter() - t0
-        if world > 1:
-            tt = torch.tensor([t_e2e], device="cuda")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t_e2e = float(tt.item())
+        t_e2e = max_over_ranks(time.perf_counter() - t0)
         e2e = {"value": round(step_bytes * args.steps / t_e2e / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": int(sum(4 * M * layer.K for layer, _, M in calls)),
                "d2h_bytes_per_step": int(sum(4 * M * layer.n_local for layer, _, M in calls)),
@@ -331,6 +344,7 @@ def run_ours(args):
                        "shapes_KN": DECODE_SHAPES, "weights": "INT8 per-channel RTN, fp16 scales",
                        "activations": "two-pass INT16 (hi_prec=1)",
                        "l2": "rotated weight copies; step working set > L2",
+                       "timing": "CUDA graph of one step (12 quantize+matmul calls), CUDA events",
                        "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -345,6 +359,7 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
 
+    del graph
     for layer in layers:
         layer.free()
     if world > 1:

@@ -101,22 +101,18 @@ Weight* allocate_weight(int N, int K, int bits, int scale_half, int has_zp) {
     w->scale_half = scale_half;
     w->has_zp = has_zp;
     w->G = N / 16;
-    w->nblkZ = (w->nblk + 1) & ~1;
+    weight_geometry(bits, scale_half != 0, has_zp != 0, &w->TB, &w->SB, &w->ZB, &w->REC);
     cudaGetDevice(&w->device);
     const size_t tiles = static_cast<size_t>(w->G) * w->nblk;
-    const size_t wb = align256(tiles * (bits == 8 ? 512 : 256));
-    const size_t sb = align256(tiles * 16 * (scale_half ? 2 : 4));
-    const size_t zb = has_zp ? align256(static_cast<size_t>(w->G) * w->nblkZ * 8) : 0;
+    const size_t bytes = align256(tiles * w->REC);
     uint8_t* base = nullptr;
-    if (cudaMalloc(&base, wb + sb + zb) != cudaSuccess) {
+    if (cudaMalloc(&base, bytes) != cudaSuccess) {
         cudaGetLastError();
         delete w;
         return nullptr;
     }
     w->W = base;
-    w->S = base + wb;
-    w->Z = has_zp ? base + wb + sb : nullptr;
-    w->bytes = wb + sb + zb;
+    w->bytes = bytes;
     return w;
 }
 
@@ -144,16 +140,16 @@ size_t ws_bytes_for(int M, int nblk) {
     return chunks * chunk_bytes(M, nblk);
 }
 
-ActView chunk_view(void* ws, int M, int nblk, int c) {
+ActView chunk_view(void* ws, int M, int nblk, int c, bool hi_prec) {
     const int m0 = c * MAX_DECODE_TOKENS;
     const int mc = std::min(MAX_DECODE_TOKENS, M - m0);
-    return act_carve(static_cast<uint8_t*>(ws) + static_cast<size_t>(c) * chunk_bytes(M, nblk), mc, nblk);
+    return act_carve(static_cast<uint8_t*>(ws) + static_cast<size_t>(c) * chunk_bytes(M, nblk), mc, nblk, hi_prec);
 }
 
 int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, bool hi_prec) {
     const int nblk = K / 32;
     for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
-        const ActView act = chunk_view(ws, M, nblk, c);
+        const ActView act = chunk_view(ws, M, nblk, c, hi_prec);
         cudaError_t e = launch_quantize_act(dA + static_cast<size_t>(c) * MAX_DECODE_TOKENS * K, K,
                                             act.M, K, hi_prec, act, stream);
         if (e != cudaSuccess) return cuda_status(e);
@@ -164,7 +160,7 @@ int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, b
 int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS, cudaStream_t stream,
                 bool hi_prec, bool pdl) {
     for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
-        const ActView act = chunk_view(const_cast<void*>(ws), M, w->nblk, c);
+        const ActView act = chunk_view(const_cast<void*>(ws), M, w->nblk, c, hi_prec);
         const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
         cudaError_t e = launch_decode(w, act, hi_prec, dC ? dC + m0 * w->N : nullptr, w->N,
                                       dCS ? dCS + m0 * w->N * w->nblk : nullptr, stream, pdl);

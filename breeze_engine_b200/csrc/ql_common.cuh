@@ -164,17 +164,35 @@ __device__ __forceinline__ uint32_t nib_odd_s8(uint32_t x, uint32_t c) {
 // mma.sync m16n8k32, A = weights (s8, 16 rows x 32 k), B = activations (8 tokens x 32 k).
 __device__ __forceinline__ void mma_s8s8(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
                  "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_s8u8(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
                  "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Same MMAs with a separate (loop-invariant) C operand: d = a*b + c.
+__device__ __forceinline__ void mma_s8s8_c(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                           uint32_t b1, const int32_t (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
+          "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+__device__ __forceinline__ void mma_s8u8_c(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                           uint32_t b1, const int32_t (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
+          "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
 }
 
 // ---------------------------------------------------------------- PDL

@@ -1,112 +1,129 @@
 // ql_gemv.cu -- decode (skinny) quantized GEMV/GEMM for M = 1..64 tokens.
 //
 // Computes C[m, n] = i4_matmul(A)[m, n] (kernel/quantized_matmul.cpp:270-318
-// tile_kernel, :320-365 tile_kernel8) from pre-quantized activations.
+// tile_kernel, :320-365 tile_kernel8) from activations quantized by ql_quant.cu.
 //
-// Design (HBM-streaming, warp specialised):
-//   * CTA = R consumer warps + 1 producer warp.  Consumer warp w owns the
-//     16-row weight group G = blockIdx.x*R + w for ALL of K, so every output's
-//     FP32 chain acc = fma(ascale, f, acc) runs in ascending block order in one
-//     thread's registers -- bit-identical to the reference, no split-K fixup.
-//   * The producer's lane 0 streams stages of BPS blocks with 1-D bulk copies
-//     (cp.async.bulk, no multicast) into a STAGES-deep shared-memory ring:
-//     per consumer the W/S/Z chunks (contiguous in the prepacked layout), and
-//     once per CTA the activation planes and scales for those blocks, shared
-//     by all R row groups.  full[]/empty[] mbarriers hand stages over.
-//   * Consumers: per block, one 16x32 weight fragment (LDS.128 INT8, LDS.64 +
-//     7 ALU ops per word INT4), then per 8-token group two m16n8k32 integer
-//     MMAs (hi plane s8 x s8, lo plane s8 x u8) seeded with the magic
-//     constants of ql_common.cuh, and four packed-f32x2 ops per two outputs
-//     for the exact rescale.
-//   * With PDL the producer issues the first weight stages before waiting on
-//     the quantizer grid (griddepcontrol.wait), overlapping its tail.
+// Warp roles in a CTA that owns R row groups of 16 output features:
+//   * producer (1 warp, lane 0): streams stage i (BPS consecutive 32-wide
+//     blocks) into a STAGES-deep shared-memory ring with 1-D bulk copies
+//     (cp.async.bulk, no multicast): ONE copy per row group (its weight records
+//     -- weights, scales and zero points of BPS blocks are contiguous) plus ONE
+//     copy of the activation records shared by the CTA.  Bulk copies cost a
+//     roughly fixed number of cycles each, so stages are large and few.
+//   * consumers (S per row group): warp (r, s) takes stages i = s, s+S, ...  Per
+//     block: one 16x32 weight fragment (LDS.128 INT8; LDS.64 + 7 integer ops
+//     per 8 nibbles INT4); per 8-token group one LDS.128 of both activation
+//     planes and two m16n8k32 integer MMAs whose C operand is the constant
+//     magic seed; then the exact f = RN((float)cs * bscale) with packed f32x2
+//     ops (ql_common.cuh).  C blocks are computed together for ILP.
+//   * exact FP32 chain: every output needs acc = fma(ascale_b, f_b, acc) in
+//     ascending block order (kernel/quantized_matmul.cpp:311-315).  The warp of
+//     stage i takes acc from the warp of stage i-1 through a shared-memory
+//     relay slot guarded by an mbarrier (all 32 lanes arrive, so every lane's
+//     store is released), applies its blocks in order and relays acc on; the
+//     warp of the last stage stores C.  Only these FFMAs are serial; the MMAs
+//     and conversions of the S warps overlap.
+// Ring slots and relay slots are always used by the same warp in phase order
+// (STAGES and the relay slot count are multiples of S), so no mbarrier waiter
+// can run two phases ahead: mbarrier.try_wait.parity would report the previous
+// phase's parity as complete.
+//
+// With PDL the producer issues the first weight stages before waiting on the
+// quantizer grid (griddepcontrol.wait).
 //
 // Template parameters: BITS (4/8), HALF (fp16 scales), ZP (explicit INT4 zero
-// points), MT (8-token groups, 1..8), HP (two-pass INT16 / single-pass INT8),
-// OUT_CS (debug: write the per-block INT32 accumulators instead of C).
+// points), MT (8-token groups: 1, 2, 4, 8), HP (two-pass INT16 / single-pass
+// INT8), OUT_CS (write the per-block INT32 accumulators instead of C).
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include "ql_common.cuh"
 #include "ql_internal.h"
 
 namespace ql {
 
 struct DecodeParams {
-    const uint8_t* W;
-    const void* S;
-    const uint8_t* Z;
-    const uint8_t* hs;
-    const uint8_t* lo;
-    const float* as;
+    const uint8_t* W;        // weight records [G][nblk][REC]
+    const uint8_t* q;        // activation records [nblk][QREC]
     float* C;
     int32_t* CS;
     int* err;
-    int M, N, nblk, nblkZ, G, ldc;
-    int R, BPS, STAGES;
+    int M, N, nblk, G, ldc;
+    int TPB, TPBA, QREC;     // activation record geometry
+    int R, SPLIT, BPS, STAGES;
     uint32_t stage_bytes;
-    uint32_t off_S, off_Z, off_H, off_L, off_A;   // offsets inside a stage
+    uint32_t off_Q;                        // activation records inside a stage
+    uint32_t off_relay, off_stages;        // offsets inside dynamic shared memory
 };
 
-template <int BITS, bool HALF, bool ZP>
-struct WeightGeom {
-    static constexpr int TB = BITS == 8 ? 512 : 256;        // tile bytes
+template <int BITS, bool HALF, bool ZP, bool HP>
+struct Geom {
+    static constexpr int TB = BITS == 8 ? 512 : 256;        // weight tile bytes
     static constexpr int SB = HALF ? 32 : 64;               // scale bytes per tile
-    static constexpr int ZB = ZP ? 8 : 0;                   // zero-point bytes per tile
+    static constexpr int ZB = ZP ? 16 : 0;                  // zero-point bytes per tile
+    static constexpr int REC = TB + SB + ZB;                // weight record bytes
+    static constexpr int LB = HP ? 16 : 8;                  // activation bytes per lane
+};
+
+// Relay slots per row group: at least 2, and SPLIT when larger (see above).
+__host__ __device__ __forceinline__ int relay_slots(int split) { return split < 2 ? 2 : split; }
+
+// Blocks computed together per sub-chunk (registers hold their f and ascale).
+// With a K split a stage is exactly one sub-chunk, so a warp computes all of
+// its stage's f values before it waits for the relay: each relay hop then
+// costs only the stage's FFMA chain and the hand-off.
+template <int MT>
+struct Chunk {
+    static constexpr int C = MT == 1 ? 16 : (MT == 2 ? 8 : (MT == 4 ? 4 : 2));
 };
 
 template <int BITS, bool HALF, bool ZP, int MT, bool HP, bool OUT_CS>
-__global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
-    using Geo = WeightGeom<BITS, HALF, ZP>;
+__global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
+    using Geo = Geom<BITS, HALF, ZP, HP>;
+    constexpr int C = Chunk<MT>::C;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                // full[STAGES], empty[STAGES]
-    uint8_t* stages = smem + 128 * ((2 * p.STAGES * 8 + 127) / 128);
+    // barriers: full[STAGES], empty[STAGES], relay[R][NS]
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty_bar = full_bar + p.STAGES;
+    uint64_t* relay_bar = empty_bar + p.STAGES;
+    uint8_t* stages = smem + p.off_stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int consumers = p.R * p.SPLIT;
+    const int NS = relay_slots(p.SPLIT);
     const int G0 = blockIdx.x * p.R;
     const int active = min(p.R, p.G - G0);
     const int nst = (p.nblk + p.BPS - 1) / p.BPS;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.STAGES; ++s) {
-            mbar_init(smem_u32(&bars[s]), 1);
-            mbar_init(smem_u32(&bars[p.STAGES + s]), active);
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), active);
         }
+        for (int k = 0; k < p.R * NS; ++k) mbar_init(smem_u32(&relay_bar[k]), 32);
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == p.R) {
+    if (warp == consumers) {
         // ------------------------------------------------------------ producer
         if (lane != 0) return;
-        const size_t act_blk = static_cast<size_t>(MT) * 256;        // plane bytes per block
         auto issue = [&](int i, bool weights, bool acts) {
             const int s = i % p.STAGES;
             const uint32_t base = smem_u32(stages + static_cast<size_t>(s) * p.stage_bytes);
-            const uint32_t full = smem_u32(&bars[s]);
+            const uint32_t full = smem_u32(&full_bar[s]);
             const int b0 = i * p.BPS;
             const int nb = min(p.BPS, p.nblk - b0);
             if (weights) {
-                // everything this stage will receive: weights/scales/zero points
-                // for each active row group, then the shared activation planes
-                // (two in two-pass mode, one in single-pass mode) and scales
-                uint32_t bytes = active * nb * (Geo::TB + Geo::SB) + (HP ? 2 : 1) * nb * act_blk +
-                                 nb * MT * 32;
-                if (ZP) bytes += active * ((nb + 1) & ~1) * 8;
-                mbar_arrive_expect_tx(full, bytes);
+                // all bytes this stage receives: each active row group's weight
+                // records plus the shared activation records
+                mbar_arrive_expect_tx(full, (active * Geo::REC + p.QREC) * nb);
                 for (int w = 0; w < active; ++w) {
-                    const size_t tile0 = static_cast<size_t>(G0 + w) * p.nblk + b0;
-                    bulk_g2s(base + w * p.BPS * Geo::TB, p.W + tile0 * Geo::TB, nb * Geo::TB, full);
-                    bulk_g2s(base + p.off_S + w * p.BPS * Geo::SB,
-                             static_cast<const uint8_t*>(p.S) + tile0 * Geo::SB, nb * Geo::SB, full);
-                    if (ZP) {
-                        const size_t z0 = (static_cast<size_t>(G0 + w) * p.nblkZ + b0) * 8;
-                        bulk_g2s(base + p.off_Z + w * p.BPS * 8, p.Z + z0, ((nb + 1) & ~1) * 8, full);
-                    }
+                    const size_t rec0 = static_cast<size_t>(G0 + w) * p.nblk + b0;
+                    bulk_g2s(base + w * p.BPS * Geo::REC, p.W + rec0 * Geo::REC, nb * Geo::REC, full);
                 }
             }
-            if (acts) {
-                if (HP) bulk_g2s(base + p.off_H, p.hs + b0 * act_blk, nb * act_blk, full);
-                bulk_g2s(base + p.off_L, p.lo + b0 * act_blk, nb * act_blk, full);
-                bulk_g2s(base + p.off_A, p.as + static_cast<size_t>(b0) * MT * 8, nb * MT * 32, full);
-            }
+            if (acts)
+                bulk_g2s(base + p.off_Q, p.q + static_cast<size_t>(b0) * p.QREC, nb * p.QREC, full);
         };
         const int first = min(p.STAGES, nst);
         for (int i = 0; i < first; ++i) issue(i, true, false);
@@ -114,137 +131,182 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
         for (int i = 0; i < first; ++i) issue(i, false, true);
         for (int i = first; i < nst; ++i) {
             const int s = i % p.STAGES;
-            if (!mbar_wait(smem_u32(&bars[p.STAGES + s]), ((i / p.STAGES) - 1) & 1, p.err)) return;
+            if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) return;
             issue(i, true, true);
         }
         return;
     }
 
     // ---------------------------------------------------------------- consumers
-    if (warp >= active) return;
-    const int G = G0 + warp;
+    const int r = warp / p.SPLIT;            // row group within the CTA
+    const int split = warp % p.SPLIT;        // stages i = split, split + SPLIT, ...
+    if (r >= active) return;
+    const int G = G0 + r;
     const int g = lane >> 2, t = lane & 3;
+    float* relay = reinterpret_cast<float*>(smem + p.off_relay) + static_cast<size_t>(r) * NS * 32 * 4 * MT;
 
-    uint64_t accA[MT], accB[MT];       // (row g | row g+8) x (tokens 2t, 2t+1) per token group
+    // Seeds as the MMA's C operand (constant registers, never overwritten).
+    const int32_t seed_h[4] = {HI_SEED, HI_SEED, HI_SEED, HI_SEED};
+    const int32_t seed_l[4] = {LO_SEED, LO_SEED, LO_SEED, LO_SEED};
+    const uint64_t negc_lo = f2_pack(-12582912.0f, -12582912.0f);   // single-pass: -1.5*2^23
+    const int qfrag = p.TPB * 4 * Geo::LB;   // scales start here inside an activation record
+
+    uint64_t accA[MT], accB[MT];             // (row g | row g+8) x (tokens 2t, 2t+1)
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) { accA[mt] = 0; accB[mt] = 0; }
 
-    const uint64_t negc_lo = f2_pack(-12582912.0f, -12582912.0f);   // single-pass: -1.5*2^23
-
-    for (int i = 0; i < nst; ++i) {
+    for (int i = split; i < nst; i += p.SPLIT) {
         const int s = i % p.STAGES;
-        if (!mbar_wait(smem_u32(&bars[s]), (i / p.STAGES) & 1, p.err)) return;
+        if (!mbar_wait(smem_u32(&full_bar[s]), (i / p.STAGES) & 1, p.err)) return;
         const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
-        const uint8_t* Wst = st + warp * p.BPS * Geo::TB;
-        const uint8_t* Sst = st + p.off_S + warp * p.BPS * Geo::SB;
-        const uint8_t* Zst = st + p.off_Z + warp * p.BPS * 8;
-        const uint8_t* Hst = st + p.off_H;
-        const uint8_t* Lst = st + p.off_L;
-        const float* Ast = reinterpret_cast<const float*>(st + p.off_A);
+        const uint8_t* Wst = st + r * p.BPS * Geo::REC;
+        const uint8_t* Qst = st + p.off_Q;
         const int b0 = i * p.BPS;
         const int nb = min(p.BPS, p.nblk - b0);
-        for (int j = 0; j < nb; ++j) {
-            // ---- weights: A fragment of the 16x32 tile
-            uint32_t a[4];
-            if (BITS == 8) {
-                const uint4 v = *reinterpret_cast<const uint4*>(Wst + j * Geo::TB + lane * 16);
-                a[0] = v.x; a[1] = v.y; a[2] = v.z; a[3] = v.w;
-            } else {
-                const uint2 v = *reinterpret_cast<const uint2*>(Wst + j * Geo::TB + lane * 8);
-                uint32_t c0 = 0x78787878u, c1 = 0x78787878u;                  // zp = 8
-                if (ZP) {
-                    const uint32_t z = Zst[j * 8 + g];
-                    c0 = (0x80u - (z & 15u)) * 0x01010101u;
-                    c1 = (0x80u - (z >> 4)) * 0x01010101u;
+        bool need_relay = !OUT_CS && p.SPLIT > 1 && i > 0;
+
+        for (int j0 = 0; j0 < nb; j0 += C) {
+            uint64_t fr[C][MT][2];           // f of C blocks (rows g, g+8)
+            uint64_t ar[C][MT];              // their activation scale pairs
+#pragma unroll
+            for (int u = 0; u < C; ++u) {
+                const int j = min(j0 + u, nb - 1);           // slots past nb are discarded
+                const uint8_t* rec = Wst + j * Geo::REC;
+                uint32_t a[4];
+                if (BITS == 8) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(rec + lane * 16);
+                    a[0] = v.x; a[1] = v.y; a[2] = v.z; a[3] = v.w;
+                } else {
+                    const uint2 v = *reinterpret_cast<const uint2*>(rec + lane * 8);
+                    uint32_t c0 = 0x78787878u, c1 = 0x78787878u;          // zp = 8
+                    if (ZP) {
+                        const uint32_t z = rec[Geo::TB + Geo::SB + g];
+                        c0 = (0x80u - (z & 15u)) * 0x01010101u;
+                        c1 = (0x80u - (z >> 4)) * 0x01010101u;
+                    }
+                    a[0] = nib_even_s8(v.x, c0);
+                    a[1] = nib_odd_s8(v.x, c1);
+                    a[2] = nib_even_s8(v.y, c0);
+                    a[3] = nib_odd_s8(v.y, c1);
                 }
-                a[0] = nib_even_s8(v.x, c0);
-                a[1] = nib_odd_s8(v.x, c1);
-                a[2] = nib_even_s8(v.y, c0);
-                a[3] = nib_odd_s8(v.y, c1);
+                float bs0, bs1;
+                if (HALF) {
+                    const __half2 hs = *reinterpret_cast<const __half2*>(rec + Geo::TB + g * 4);
+                    bs0 = __low2float(hs);
+                    bs1 = __high2float(hs);
+                } else {
+                    const float2 f = *reinterpret_cast<const float2*>(rec + Geo::TB + g * 8);
+                    bs0 = f.x;
+                    bs1 = f.y;
+                }
+                const uint64_t bsA = f2_pack(bs0, bs0), bsB = f2_pack(bs1, bs1);
+                const uint8_t* qrec = Qst + j * p.QREC;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const int tok = mt * 8 + g;               // this lane's B-fragment token
+                    int32_t h[4], l[4];
+                    if (HP) {
+                        uint4 qv = make_uint4(0, 0, 0, 0);
+                        if (MT > 1 || tok < p.TPB)
+                            qv = *reinterpret_cast<const uint4*>(qrec + (tok * 4 + t) * 16);
+                        mma_s8s8_c(h, a, qv.x, qv.y, seed_h);    // hi - 128 plane
+                        mma_s8u8_c(l, a, qv.z, qv.w, seed_l);    // lo plane
+                    } else {
+                        uint2 qv = make_uint2(0, 0);
+                        if (MT > 1 || tok < p.TPB)
+                            qv = *reinterpret_cast<const uint2*>(qrec + (tok * 4 + t) * 8);
+                        mma_s8s8_c(l, a, qv.x, qv.y, seed_l);
+                    }
+                    if (OUT_CS) {
+                        if (j0 + u < nb) {
+                            const int tok0 = mt * 8 + 2 * t;
+                            const int n0 = G * 16 + g;
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int tk = tok0 + (e & 1);
+                                const int n = n0 + 8 * (e >> 1);
+                                const int32_t cs = HP ? (h[e] - HI_SEED) * 256 + (l[e] - LO_SEED)
+                                                      : l[e] - LO_SEED;
+                                if (tk < p.M)
+                                    p.CS[(static_cast<size_t>(tk) * p.N + n) * p.nblk + b0 + j] = cs;
+                            }
+                        }
+                        continue;
+                    }
+                    uint64_t yA, yB;
+                    if (HP) {
+                        yA = cs_to_f2(h[0], h[1], l[0], l[1]);
+                        yB = cs_to_f2(h[2], h[3], l[2], l[3]);
+                    } else {
+                        yA = f2_add(i2_pack(l[0], l[1]), negc_lo);   // exact (|cs| < 2^22)
+                        yB = f2_add(i2_pack(l[2], l[3]), negc_lo);
+                    }
+                    fr[u][mt][0] = f2_mul(yA, bsA);
+                    fr[u][mt][1] = f2_mul(yB, bsB);
+                    // activation scales of tokens 2t, 2t+1 (TPBA is a multiple of
+                    // 4, so both or neither exist; padded scales are zero)
+                    const int tk = mt * 8 + 2 * t;
+                    ar[u][mt] = tk < p.TPBA ? *reinterpret_cast<const uint64_t*>(qrec + qfrag + tk * 4) : 0;
+                }
             }
-            // ---- weight scales for rows g and g+8
-            float bs0, bs1;
-            if (HALF) {
-                const __half2 h = *reinterpret_cast<const __half2*>(Sst + j * Geo::SB + g * 4);
-                bs0 = __low2float(h);
-                bs1 = __high2float(h);
-            } else {
-                const float2 f = *reinterpret_cast<const float2*>(Sst + j * Geo::SB + g * 8);
-                bs0 = f.x;
-                bs1 = f.y;
+            if (OUT_CS) continue;
+            // ---- take the running accumulator of stage i-1 (once per stage)
+            if (need_relay) {
+                need_relay = false;
+                const int slot = (i - 1) % NS;
+                if (!mbar_wait(smem_u32(&relay_bar[r * NS + slot]), ((i - 1) / NS) & 1, p.err)) return;
+                const float* src = relay + (slot * 32 + lane) * 4 * MT;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const float4 v = *reinterpret_cast<const float4*>(src + 4 * mt);
+                    accA[mt] = f2_pack(v.x, v.y);
+                    accB[mt] = f2_pack(v.z, v.w);
+                }
             }
-            const uint64_t bsA = f2_pack(bs0, bs0), bsB = f2_pack(bs1, bs1);
+            // ---- the FP32 chain over these C blocks, ascending order
+#pragma unroll
+            for (int u = 0; u < C; ++u) {
+                if (j0 + u >= nb) break;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    accA[mt] = f2_fma(ar[u][mt], fr[u][mt][0], accA[mt]);
+                    accB[mt] = f2_fma(ar[u][mt], fr[u][mt][1], accB[mt]);
+                }
+            }
+        }
+        // release the stage to the producer
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+        if (OUT_CS) continue;
+        if (p.SPLIT > 1 && i + 1 < nst) {
+            // hand the accumulator to the warp of stage i + 1
+            const int slot = i % NS;
+            float* dst = relay + (slot * 32 + lane) * 4 * MT;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-                const int off = (j * MT + mt) * 256 + g * 16 + t * 4;
-                int32_t l[4] = {LO_SEED, LO_SEED, LO_SEED, LO_SEED};
-                const uint32_t l0 = *reinterpret_cast<const uint32_t*>(Lst + off);
-                const uint32_t l1 = *reinterpret_cast<const uint32_t*>(Lst + off + 128);
-                uint64_t yA, yB;
-                if (HP) {
-                    int32_t h[4] = {HI_SEED, HI_SEED, HI_SEED, HI_SEED};
-                    const uint32_t h0 = *reinterpret_cast<const uint32_t*>(Hst + off);
-                    const uint32_t h1 = *reinterpret_cast<const uint32_t*>(Hst + off + 128);
-                    mma_s8s8(h, a, h0, h1);
-                    mma_s8u8(l, a, l0, l1);
-                    if (OUT_CS) {
-                        const int tok0 = mt * 8 + 2 * t;
-                        const int n0 = G * 16 + g;
-                        const int b = b0 + j;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int tok = tok0 + (e & 1);
-                            const int n = n0 + 8 * (e >> 1);
-                            if (tok < p.M)
-                                p.CS[(static_cast<size_t>(tok) * p.N + n) * p.nblk + b] =
-                                    (h[e] - HI_SEED) * 256 + (l[e] - LO_SEED);
-                        }
-                        continue;
-                    }
-                    yA = cs_to_f2(h[0], h[1], l[0], l[1]);
-                    yB = cs_to_f2(h[2], h[3], l[2], l[3]);
-                } else {
-                    mma_s8s8(l, a, l0, l1);
-                    if (OUT_CS) {
-                        const int tok0 = mt * 8 + 2 * t;
-                        const int n0 = G * 16 + g;
-                        const int b = b0 + j;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int tok = tok0 + (e & 1);
-                            const int n = n0 + 8 * (e >> 1);
-                            if (tok < p.M)
-                                p.CS[(static_cast<size_t>(tok) * p.N + n) * p.nblk + b] = l[e] - LO_SEED;
-                        }
-                        continue;
-                    }
-                    yA = f2_add(i2_pack(l[0], l[1]), negc_lo);     // exact (|cs| < 2^22)
-                    yB = f2_add(i2_pack(l[2], l[3]), negc_lo);
-                }
-                const float2 asv = *reinterpret_cast<const float2*>(Ast + (j * MT + mt) * 8 + 2 * t);
-                const uint64_t as2 = f2_pack(asv.x, asv.y);
-                accA[mt] = f2_fma(as2, f2_mul(yA, bsA), accA[mt]);
-                accB[mt] = f2_fma(as2, f2_mul(yB, bsB), accB[mt]);
+                const float2 A2 = f2_unpack(accA[mt]);
+                const float2 B2 = f2_unpack(accB[mt]);
+                *reinterpret_cast<float4*>(dst + 4 * mt) = make_float4(A2.x, A2.y, B2.x, B2.y);
             }
+            mbar_arrive(smem_u32(&relay_bar[r * NS + slot]));
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&bars[p.STAGES + s]));
-    }
-
-    if (OUT_CS) return;
-    const int n0 = G * 16 + g;
+        if (i + 1 >= nst) {
+            // this warp ran the last stage: store the outputs
+            const int n0 = G * 16 + g;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-        const int tok0 = mt * 8 + 2 * t;
-        const float2 A2 = f2_unpack(accA[mt]);
-        const float2 B2 = f2_unpack(accB[mt]);
-        if (tok0 < p.M) {
-            p.C[static_cast<size_t>(tok0) * p.ldc + n0] = A2.x;
-            p.C[static_cast<size_t>(tok0) * p.ldc + n0 + 8] = B2.x;
-        }
-        if (tok0 + 1 < p.M) {
-            p.C[static_cast<size_t>(tok0 + 1) * p.ldc + n0] = A2.y;
-            p.C[static_cast<size_t>(tok0 + 1) * p.ldc + n0 + 8] = B2.y;
+            for (int mt = 0; mt < MT; ++mt) {
+                const int tok0 = mt * 8 + 2 * t;
+                const float2 A2 = f2_unpack(accA[mt]);
+                const float2 B2 = f2_unpack(accB[mt]);
+                if (tok0 < p.M) {
+                    p.C[static_cast<size_t>(tok0) * p.ldc + n0] = A2.x;
+                    p.C[static_cast<size_t>(tok0) * p.ldc + n0 + 8] = B2.x;
+                }
+                if (tok0 + 1 < p.M) {
+                    p.C[static_cast<size_t>(tok0 + 1) * p.ldc + n0] = A2.y;
+                    p.C[static_cast<size_t>(tok0 + 1) * p.ldc + n0 + 8] = B2.y;
+                }
+            }
         }
     }
 }
@@ -252,20 +314,17 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
 // ------------------------------------------------------------------ host side
 
 struct DecodeConfig {
-    int R, BPS, STAGES;
+    int R, SPLIT, BPS, STAGES;
 };
 
 static int g_num_sms = 0;
+constexpr int SMEM_BUDGET = 110 * 1024;   // dynamic shared memory per CTA: >= 2 CTAs per SM
 
-constexpr int SMEM_BUDGET = 200 * 1024;   // dynamic shared memory per CTA (of 227 KB)
-
-// Exact bytes of one ring stage (must match the carve-up in launch_t).
-static int stage_bytes_for(int R, int BPS, int MT, int tb, int sb, bool zp, bool hp) {
-    const int b = R * BPS * (tb + sb + (zp ? 8 : 0)) + (hp ? 2 : 1) * BPS * MT * 256 + BPS * MT * 32;
-    return (b + 127) & ~127;
+static int stage_bytes_for(int R, int BPS, int rec, int qrec) {
+    return (R * BPS * rec + BPS * qrec + 127) & ~127;
 }
 
-static DecodeConfig choose_config(int G, int nblk, int MT, int tb, int sb, bool zp, bool hp) {
+static DecodeConfig choose_config(int G, int nblk, int C, int rec, int qrec) {
     if (g_num_sms == 0) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -273,50 +332,90 @@ static DecodeConfig choose_config(int G, int nblk, int MT, int tb, int sb, bool 
         if (g_num_sms <= 0) g_num_sms = 148;
     }
     DecodeConfig c;
-    // Enough CTAs for ~2 per SM, as many row groups per CTA as that allows
-    // (activation stages are shared by the R row groups of a CTA).
+    // ~12 consumer warps per SM in total: row groups first, then K splits.
+    const long long target = 12LL * g_num_sms;
+    // (Measured on B200: 4 row groups per CTA without a split win from ~600
+    // row groups up; below that, split K across 4 warps per row group.)
     c.R = 1;
-    if (G >= 4 * 2 * g_num_sms) c.R = 4;
-    else if (G >= 2 * 2 * g_num_sms) c.R = 2;
-    // Stage: BPS blocks (even); aim for ~32 KB of copies in flight per CTA,
-    // at least 2 stages, and stay inside the shared-memory budget.
-    c.BPS = (c.R == 1) ? 16 : 8;
+    c.SPLIT = 1;
+    if (G >= 4 * g_num_sms) c.R = 4;
+    else if (G >= 2 * g_num_sms) c.R = 2;
+    while (c.R <= 2 && c.SPLIT < 8 && c.R * c.SPLIT < 8 && static_cast<long long>(G) * c.SPLIT * 2 <= target)
+        c.SPLIT *= 2;
     const int nblk_even = (nblk + 1) & ~1;
-    if (c.BPS > nblk_even) c.BPS = nblk_even;
-    if (c.BPS < 2) c.BPS = 2;
-    while (c.BPS > 2 && 2 * stage_bytes_for(c.R, c.BPS, MT, tb, sb, zp, hp) > SMEM_BUDGET) c.BPS -= 2;
-    const int st = stage_bytes_for(c.R, c.BPS, MT, tb, sb, zp, hp);
-    c.STAGES = std::max(3, std::min(8, 32768 / st));
-    while (c.STAGES > 2 && c.STAGES * st > SMEM_BUDGET) --c.STAGES;
+    // A split stage is one sub-chunk (C blocks); at least two stages per split.
+    while (c.SPLIT > 1 && (nblk_even + C - 1) / C < 2 * c.SPLIT) c.SPLIT /= 2;
+    if (c.SPLIT > 1) {
+        c.BPS = C;
+    } else {
+        // Stages of >= 32 KB (bulk copies have a fixed cost each), two of
+        // which must fit the shared-memory budget.
+        c.BPS = C;
+        while (c.BPS < 32 && stage_bytes_for(c.R, c.BPS, rec, qrec) < 32768 &&
+               2 * stage_bytes_for(c.R, c.BPS + C, rec, qrec) <= SMEM_BUDGET)
+            c.BPS += C;
+    }
+    if (c.BPS > nblk_even) c.BPS = std::max(2, ((nblk_even + C - 1) / C) * C);
+    const int st = stage_bytes_for(c.R, c.BPS, rec, qrec);
+    // ~48 KB in flight per CTA, >= 2 stages per split, a multiple of SPLIT.
+    c.STAGES = std::max(2 * c.SPLIT, (49152 + st - 1) / st);
+    c.STAGES = std::min(c.STAGES, std::max(2 * c.SPLIT, 8));
+    c.STAGES = ((c.STAGES + c.SPLIT - 1) / c.SPLIT) * c.SPLIT;
+    if (c.STAGES < 2) c.STAGES = 2;
+    while (c.STAGES - c.SPLIT >= std::max(2, c.SPLIT) && c.STAGES * st > SMEM_BUDGET) c.STAGES -= c.SPLIT;
+    // Tuning override "R,SPLIT,BPS,STAGES" (each 0 = keep the planner's choice).
+    // Values that break the planner's invariants are rejected by launch_t.
+    if (const char* env = std::getenv("BREEZE_QL_DECODE_CONFIG")) {
+        int r = 0, sp = 0, b = 0, s = 0;
+        if (std::sscanf(env, "%d,%d,%d,%d", &r, &sp, &b, &s) == 4) {
+            if (r > 0) c.R = r;
+            if (sp > 0) c.SPLIT = sp;
+            if (b > 0) c.BPS = b;
+            if (s > 0) c.STAGES = s;
+        }
+    }
     return c;
 }
 
 template <int BITS, bool HALF, bool ZP, int MT, bool HP, bool OUT_CS>
 static cudaError_t launch_t(const DecodeParams& p0, const DecodeConfig& c, cudaStream_t stream, bool pdl) {
-    using Geo = WeightGeom<BITS, HALF, ZP>;
+    using Geo = Geom<BITS, HALF, ZP, HP>;
+    constexpr int C = Chunk<MT>::C;
     DecodeParams p = p0;
     p.R = c.R;
+    p.SPLIT = c.SPLIT;
     p.BPS = c.BPS;
     p.STAGES = c.STAGES;
-    uint32_t off = c.R * c.BPS * Geo::TB;
-    p.off_S = off;  off += c.R * c.BPS * Geo::SB;
-    p.off_Z = off;  off += ZP ? c.R * c.BPS * 8 : 0;
-    p.off_H = off;  off += HP ? c.BPS * MT * 256 : 0;
-    p.off_L = off;  off += c.BPS * MT * 256;
-    p.off_A = off;  off += c.BPS * MT * 32;
-    p.stage_bytes = (off + 127) & ~127u;
-    const size_t smem = 128 * ((2 * c.STAGES * 8 + 127) / 128) + static_cast<size_t>(c.STAGES) * p.stage_bytes;
-    // Host-side guards: the carve-up must match the planner and fit the SM.
-    if (static_cast<int>(p.stage_bytes) != stage_bytes_for(c.R, c.BPS, MT, Geo::TB, Geo::SB, ZP, HP) ||
-        smem > 227 * 1024 || c.BPS < 2 || (c.BPS & 1) || c.STAGES < 2 || c.R < 1 || c.R > 4)
+    p.off_Q = c.R * c.BPS * Geo::REC;
+    p.stage_bytes = stage_bytes_for(c.R, c.BPS, Geo::REC, p.QREC);
+    const int NS = relay_slots(c.SPLIT);
+    const uint32_t bar_bytes = (2 * c.STAGES + c.R * NS) * 8;
+    p.off_relay = (bar_bytes + 127) & ~127u;
+    const uint32_t relay_bytes = c.R * NS * 32 * 4 * MT * 4;
+    p.off_stages = (p.off_relay + relay_bytes + 127) & ~127u;
+    const size_t smem = p.off_stages + static_cast<size_t>(c.STAGES) * p.stage_bytes;
+    // Host-side guards: the carve-up must fit the SM and keep the invariants
+    // the kernel relies on (16-byte copies, slots owned by one warp).
+    const int consumers = c.R * c.SPLIT;
+    if (smem > 227 * 1024 || c.BPS < 2 || (c.BPS % C) || c.STAGES < 2 || c.R < 1 || c.R > 8 ||
+        c.SPLIT < 1 || c.SPLIT > 8 || consumers > 8 || (c.STAGES % c.SPLIT) || (p.QREC % 16) ||
+        (Geo::REC % 16) || (p.off_Q % 16))
         return cudaErrorInvalidConfiguration;
     auto kern = decode_kernel<BITS, HALF, ZP, MT, HP, OUT_CS>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
+    // Raise the dynamic shared-memory limit once per instantiation and device,
+    // so launches captured into a CUDA graph make no attribute calls.
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (configured[dev] < static_cast<int>(smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 227 * 1024;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.G + c.R - 1) / c.R);
-    cfg.blockDim = dim3(32 * (c.R + 1));
+    cfg.blockDim = dim3(32 * (consumers + 1));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -329,13 +428,13 @@ static cudaError_t launch_t(const DecodeParams& p0, const DecodeConfig& c, cudaS
 
 template <int BITS, bool HALF, bool ZP, bool HP, bool OUT_CS>
 static cudaError_t dispatch_mt(const DecodeParams& p, int MT, cudaStream_t stream, bool pdl) {
-    using Geo = WeightGeom<BITS, HALF, ZP>;
-    const DecodeConfig c = choose_config(p.G, p.nblk, MT, Geo::TB, Geo::SB, ZP, HP);
+    using Geo = Geom<BITS, HALF, ZP, HP>;
+    auto cfg = [&](int C) { return choose_config(p.G, p.nblk, C, Geo::REC, p.QREC); };
     switch (MT) {
-        case 1: return launch_t<BITS, HALF, ZP, 1, HP, OUT_CS>(p, c, stream, pdl);
-        case 2: return launch_t<BITS, HALF, ZP, 2, HP, OUT_CS>(p, c, stream, pdl);
-        case 4: return launch_t<BITS, HALF, ZP, 4, HP, OUT_CS>(p, c, stream, pdl);
-        default: return launch_t<BITS, HALF, ZP, 8, HP, OUT_CS>(p, c, stream, pdl);
+        case 1: return launch_t<BITS, HALF, ZP, 1, HP, OUT_CS>(p, cfg(Chunk<1>::C), stream, pdl);
+        case 2: return launch_t<BITS, HALF, ZP, 2, HP, OUT_CS>(p, cfg(Chunk<2>::C), stream, pdl);
+        case 4: return launch_t<BITS, HALF, ZP, 4, HP, OUT_CS>(p, cfg(Chunk<4>::C), stream, pdl);
+        default: return launch_t<BITS, HALF, ZP, 8, HP, OUT_CS>(p, cfg(Chunk<8>::C), stream, pdl);
     }
 }
 
@@ -358,26 +457,26 @@ int* device_error_word();   // ql_api.cu
 
 cudaError_t launch_decode(const Weight* w, const ActView& act, bool hi_prec, float* C, int ldc,
                           int32_t* cs, cudaStream_t stream, bool pdl) {
+    if (act.hp != (hi_prec ? 1 : 0)) return cudaErrorInvalidValue;   // layout depends on the mode
     DecodeParams p = {};
     p.W = w->W;
-    p.S = w->S;
-    p.Z = w->Z;
-    p.hs = act.hs;
-    p.lo = act.lo;
-    p.as = act.as;
+    p.q = act.q;
     p.C = C;
     p.CS = cs;
     p.err = device_error_word();
     p.M = act.M;
     p.N = w->N;
     p.nblk = w->nblk;
-    p.nblkZ = w->nblkZ;
     p.G = w->G;
     p.ldc = ldc;
-    // The kernel's activation stride per block is MT*256: the token-group
-    // count of the template must equal the workspace's.
+    p.TPB = act.TPB;
+    p.TPBA = act.TPBA;
+    p.QREC = act.QREC;
     const int MT = act.MT;
     if (MT != 1 && MT != 2 && MT != 4 && MT != 8) return cudaErrorInvalidValue;
+    if ((MT == 1 && (act.TPB < 1 || act.TPB > 8)) || (MT > 1 && act.TPB != 8 * MT) ||
+        act.TPBA < act.TPB || (act.TPBA & 3) || act.QREC != act.TPB * 4 * act.LB + act.TPBA * 4)
+        return cudaErrorInvalidValue;
     if (cs) {
         return hi_prec ? dispatch_w<true, true>(w, p, MT, stream, pdl)
                        : dispatch_w<false, true>(w, p, MT, stream, pdl);

@@ -8,52 +8,68 @@ namespace ql {
 
 // Device-resident packed weight (the opaque handle behind void*).
 //
-// HBM layout (all arrays 256-byte aligned, G = N/16 row groups):
-//   W  [G][nblk][TB]    TB = 256 (INT4) or 512 (INT8).  One 16-row x 32-k tile
-//                       per (group, block) in mma.sync m16n8k32 A-fragment order:
+// HBM layout: one record per (16-row group, 32-wide K block), records of a row
+// group contiguous in K order, so a stage of any number of blocks of one row
+// group is ONE contiguous bulk copy:
+//   rec[G][nblk][REC]   REC = TB + SB + ZB bytes (a multiple of 16):
+//     [0, TB)           16x32 tile in mma.sync m16n8k32 A-fragment order:
 //                       lane L = 4g + t owns rows {g, g+8} x k {4t..4t+3, 16+4t..16+4t+3}.
 //                       INT8: 16 bytes per lane, byte = q ^ 0x80 (= q - 128, signed).
 //                       INT4: 8 bytes per lane, raw nibbles q; word 0 interleaves
 //                       (row g, row g+8) for k 4t..4t+3, word 1 the same for k+16.
-//   S  [G][nblk][16]    block scales, entry 2g = row g, 2g+1 = row g+8; kept as
-//                       the caller's fp16 bits (exact widening on use) or fp32.
-//   Z  [G][nblkZ][8]    INT4 explicit zero points only: byte g = zp(g) | zp(g+8) << 4;
-//                       nblkZ = nblk rounded up to even (16-byte bulk copies).
+//                       TB = 512 (INT8) or 256 (INT4).
+//     [TB, TB+SB)       16 block scales, entry 2g = row g, 2g+1 = row g+8; the
+//                       caller's fp16 bits (SB = 32) or fp32 (SB = 64).
+//     [TB+SB, REC)      INT4 explicit zero points only (ZB = 16): byte g =
+//                       zp(g) | zp(g+8) << 4 for g < 8, then 8 padding bytes.
 struct Weight {
     uint32_t magic;
     int N, K, nblk, bits;
-    int scale_half;       // 1: S holds fp16, 0: fp32
+    int scale_half;       // 1: fp16 scales, 0: fp32
     int has_zp;           // INT4 with explicit zero points
     int device;
-    int G, nblkZ;
-    uint8_t* W;
-    void* S;
-    uint8_t* Z;
+    int G;                // N / 16 row groups
+    int TB, SB, ZB, REC;  // record geometry (bytes)
+    uint8_t* W;           // records
     size_t bytes;         // device bytes owned
 };
 
-constexpr uint32_t WEIGHT_MAGIC = 0x51574231u;   // "QWB1"
+constexpr uint32_t WEIGHT_MAGIC = 0x51574232u;   // "QWB2"
 
 inline bool valid_weight(const void* h) {
     return h && static_cast<const Weight*>(h)->magic == WEIGHT_MAGIC;
 }
 
-// Quantized activations in the kernels' layout (scratch produced per call).
-//   hs [nblk][MT][2][8][16]  hi plane as signed bytes (hi - 128); unused in
-//                            INT8 single-pass mode.
-//   lo [nblk][MT][2][8][16]  lo plane (unsigned) or, in single-pass mode, q8 (signed).
-//   as [nblk][8*MT]          activation block scales (fp32).
-// Token m lives in token group m/8, row m%8; [2] is the 16-byte K half.
-// Padded tokens (M..8*MT-1) are written as zeros.
+inline void weight_geometry(int bits, bool scale_half, bool has_zp, int* TB, int* SB, int* ZB, int* REC) {
+    *TB = bits == 8 ? 512 : 256;
+    *SB = scale_half ? 32 : 64;
+    *ZB = has_zp ? 16 : 0;
+    *REC = *TB + *SB + *ZB;
+}
+
+// Quantized activations in the kernels' layout (scratch produced per call):
+// one record per 32-wide K block, so a stage of blocks is one bulk copy.
+//   rec[nblk][QREC]            QREC = TPB*4*LB + TPBA*4 bytes
+//     [0, TPB*4*LB)            fragments of token m at m*4*LB: slot t holds what
+//                              lane 4*(m%8)+t needs as its m16n8k32 B fragment --
+//                              two-pass (LB = 16): hi-128 (signed) of k 4t..4t+3
+//                              and 16+4t..16+4t+3, then lo (unsigned) of the same
+//                              k; single-pass (LB = 8): q8 (signed) of those k.
+//     [TPB*4*LB, QREC)         fp32 activation scales of tokens 0..TPBA-1.
+// MT = token groups of 8 (1, 2, 4 or 8).  TPB = M when MT == 1 (only the real
+// tokens are stored and copied) else 8*MT; TPBA = TPB rounded up to 4.
+// Padded tokens (M..TPB-1, and scales up to TPBA) are written as zeros.
 struct ActView {
-    uint8_t* hs;
-    uint8_t* lo;
-    float* as;
+    uint8_t* q;
     int M, MT, nblk;
+    int TPB, TPBA;
+    int LB;               // bytes per fragment slot (16 two-pass, 8 single-pass)
+    int QREC;             // record bytes per block
+    int hp;               // layout/mode the records were written in
 };
 
 size_t act_bytes(int M, int nblk);                       // one chunk of M <= 64 tokens
-ActView act_carve(void* ws, int M, int nblk);
+ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 

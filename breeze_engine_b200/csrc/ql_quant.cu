@@ -33,24 +33,27 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     // still waits for this grid's completion before reading the planes.
     pdl_launch_dependents();
     const int nblk = K / BLOCK_K;
-    const int Mpad = out.MT * 8;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<long long>(Mpad) * nblk) return;
+    if (idx >= static_cast<long long>(out.TPBA) * nblk) return;
     const int m = static_cast<int>(idx / nblk);
     const int b = static_cast<int>(idx % nblk);
 
-    // [b][m/8][khalf][m%8][16]
-    const size_t grp = (static_cast<size_t>(b) * out.MT + (m >> 3)) * 256 + (m & 7) * 16;
-    uint4* hs0 = reinterpret_cast<uint4*>(out.hs + grp);
-    uint4* hs1 = reinterpret_cast<uint4*>(out.hs + grp + 128);
-    uint4* lo0 = reinterpret_cast<uint4*>(out.lo + grp);
-    uint4* lo1 = reinterpret_cast<uint4*>(out.lo + grp + 128);
+    // Block b's record: fragment slots t = 0..3 of token m (lanes 4*(m%8) + t),
+    // then the block's activation scales.
+    constexpr int LB = HP ? 16 : 8;                                   // bytes per lane
+    uint8_t* rec = out.q + static_cast<size_t>(b) * out.QREC;
+    uint8_t* frag = rec + m * 4 * LB;
+    float* scales = reinterpret_cast<float*>(rec + out.TPB * 4 * LB);
 
     if (m >= M) {   // padded token rows
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        if (HP) { *hs0 = z; *hs1 = z; }
-        *lo0 = z; *lo1 = z;
-        out.as[static_cast<size_t>(b) * Mpad + m] = 0.0f;
+        if (m < out.TPB) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                if (HP) *reinterpret_cast<uint4*>(frag + t * LB) = make_uint4(0, 0, 0, 0);
+                else *reinterpret_cast<uint2*>(frag + t * LB) = make_uint2(0, 0);
+            }
+        }
+        scales[m] = 0.0f;
         return;
     }
 
@@ -71,7 +74,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     constexpr int IMAX = HP ? 32767 : 127;
     const float scale = __fdiv_rn(amax, QMAX);
     const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    out.as[static_cast<size_t>(b) * Mpad + m] = scale;
+    scales[m] = scale;
 
     uint32_t hw[8], lw[8];
 #pragma unroll
@@ -92,12 +95,12 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
         hw[w] = hword;
         lw[w] = lword;
     }
-    if (HP) {
-        *hs0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *hs1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    // lane t: k 4t..4t+3 (word t) and 16+4t..16+4t+3 (word 4+t) of each plane
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        if (HP) *reinterpret_cast<uint4*>(frag + t * LB) = make_uint4(hw[t], hw[4 + t], lw[t], lw[4 + t]);
+        else *reinterpret_cast<uint2*>(frag + t * LB) = make_uint2(lw[t], lw[4 + t]);
     }
-    *lo0 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    *lo1 = make_uint4(lw[4], lw[5], lw[6], lw[7]);
 }
 
 // Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
@@ -135,29 +138,32 @@ static int act_groups(int M) {
     const int mt = (M + 7) / 8;
     return mt <= 1 ? 1 : mt <= 2 ? 2 : mt <= 4 ? 4 : 8;
 }
+static int act_tpb(int M) { return act_groups(M) == 1 ? M : 8 * act_groups(M); }
+static int act_tpba(int M) { return (act_tpb(M) + 3) & ~3; }
 
+// Sized for the two-pass layout (the larger one) whatever the mode.
 size_t act_bytes(int M, int nblk) {
-    const size_t MT = static_cast<size_t>(act_groups(M));
-    const size_t plane = (static_cast<size_t>(nblk) * MT * 256 + 255) & ~size_t(255);
-    const size_t as = (static_cast<size_t>(nblk) * MT * 8 * 4 + 255) & ~size_t(255);
-    return 2 * plane + as;
+    const size_t rec = static_cast<size_t>(act_tpb(M)) * 64 + act_tpba(M) * 4;
+    return (static_cast<size_t>(nblk) * rec + 255) & ~size_t(255);
 }
 
-ActView act_carve(void* ws, int M, int nblk) {
+ActView act_carve(void* ws, int M, int nblk, bool hi_prec) {
     ActView v;
     v.M = M;
     v.MT = act_groups(M);
+    v.TPB = act_tpb(M);
+    v.TPBA = act_tpba(M);
     v.nblk = nblk;
-    const size_t plane = (static_cast<size_t>(nblk) * v.MT * 256 + 255) & ~size_t(255);
-    v.hs = static_cast<uint8_t*>(ws);
-    v.lo = v.hs + plane;
-    v.as = reinterpret_cast<float*>(v.lo + plane);
+    v.hp = hi_prec ? 1 : 0;
+    v.LB = hi_prec ? 16 : 8;
+    v.QREC = v.TPB * 4 * v.LB + v.TPBA * 4;
+    v.q = static_cast<uint8_t*>(ws);
     return v;
 }
 
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
                                 const ActView& out, cudaStream_t stream) {
-    const long long total = static_cast<long long>(out.MT) * 8 * (K / BLOCK_K);
+    const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     if (hi_prec)

@@ -32,7 +32,16 @@ def cases():
 
 
 def bits_equal(a, b):
-    """Bit-for-bit equality of float32 arrays (NaN payloads included)."""
+    """Bit-for-bit equality of float32 arrays, with NaN exactly where the other
+    has NaN.  NaN payloads are not compared: x86 produces its default NaN
+    0xFFC00000 for an invalid operation (inf * 0), CUDA the canonical
+    0x7FFFFFFF; every non-NaN value, signed zeros and infinities included,
+    must match bit for bit."""
     a = np.ascontiguousarray(a, np.float32)
     b = np.ascontiguousarray(b, np.float32)
-    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    if a.shape != b.shape:
+        return False
+    na, nb = np.isnan(a), np.isnan(b)
+    if not np.array_equal(na, nb):
+        return False
+    return np.array_equal(a.view(np.uint32)[~na], b.view(np.uint32)[~nb])
