@@ -11,7 +11,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("BREEZE_B200_KERNEL", os.path.join(HERE, "libbreeze_ql.so"))
 
-QL_OK, QL_EINVAL, QL_ENOMEM, QL_ECUDA, QL_ETIMEOUT, QL_EDEVICE, QL_ENOTSUP = range(7)
+QL_OK, QL_EINVAL, QL_ENOMEM, QL_ECUDA, QL_ETIMEOUT, QL_EDEVICE, QL_ENOTSUP, QL_ESCRATCH = range(8)
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -39,6 +39,7 @@ SIGNATURES = [
     ("ql_workspace_bytes", _sz, [_vp, _i]),
     ("ql_matmul_dev_ws", _i, [_vp, _vp, _i, _vp, _vp, _sz, _vp]),
     ("ql_matmul_dev", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ql_matmul_dev_noalloc", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ql_act_workspace_bytes", _sz, [_i, _i]),
     ("ql_quantize_act_dev", _i, [_vp, _i, _i, _i, _vp, _sz, _vp]),
     ("ql_matmul_quantized_dev", _i, [_vp, _vp, _i, _i, _vp, _vp]),

@@ -247,6 +247,7 @@ QL_API const char* ql_error_string(int code) {
         case QL_ETIMEOUT: return "bounded device wait timed out";
         case QL_EDEVICE: return "handle belongs to another device";
         case QL_ENOTSUP: return "unsupported configuration";
+        case QL_ESCRATCH: return "request exceeds the fixed scratch of ql_matmul_dev_noalloc";
         default: return "unknown error";
     }
 }
@@ -499,6 +500,54 @@ QL_API int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_p
     const auto* w = static_cast<const Weight*>(handle);
     if (dev != w->device) return set_status(QL_EDEVICE);
     return run_compute(w, ws, M, dC, nullptr, static_cast<cudaStream_t>(stream), hi_prec != 0, false);
+}
+
+// ------------------------------------------------------------------ no-allocation variant
+//
+// Some callers cannot allocate device memory at the time they run a layer:
+// code that is being captured into a CUDA graph (cudaMalloc is not allowed
+// during stream capture), serving runtimes whose allocator owns all of HBM
+// (weights and KV cache are reserved up front and nothing else may allocate),
+// and per-token decode loops that cannot pay for an allocation or for the
+// device-wide synchronisation that freeing one implies.  For them,
+// ql_matmul_dev_noalloc keeps the quantized activations in a fixed scratch
+// array compiled into this library instead of a workspace.
+//
+// The array is a file-scope __device__ variable: every GPU that loads the
+// library holds these QL_NOALLOC_SCRATCH_BYTES until the process exits.  Host
+// code cannot use the symbol as an address, so the first call on each device
+// (with that device current) looks up its device address once with
+// cudaGetSymbolAddress and caches it; make that first call before any stream
+// capture.  All calls share the one array and it keeps the last call's
+// contents; nothing needs to start at zero, because the quantizer writes every
+// byte the matmul reads (padded token rows included).  Calls whose work
+// overlaps on the GPU (different streams, or a second call before the first
+// finished on another stream) race on the array: serialise them.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[QL_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_addr[MAX_DEVICES] = {};
+}  // namespace
+
+QL_API int ql_matmul_dev_noalloc(void* handle, const float* dA, int M, float* dC, void* stream) {
+    const int c = check_call(handle, dA, M, dC);
+    if (c != QL_OK || M == 0) return set_status(c);
+    const auto* w = static_cast<const Weight*>(handle);
+    if (ws_bytes_for(M, w->nblk) > QL_NOALLOC_SCRATCH_BYTES) return set_status(QL_ESCRATCH);
+    const bool hp = ql_get_hi_prec() != 0;
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_noalloc_addr[w->device]) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || !p) return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+            g_noalloc_addr[w->device] = p;
+        }
+        scratch = g_noalloc_addr[w->device];
+    }
+    return run_matmul(w, dA, M, dC, nullptr, scratch, QL_NOALLOC_SCRATCH_BYTES,
+                      static_cast<cudaStream_t>(stream), hp);
 }
 
 // Per-block INT32 accumulators cs[M][N][K/32] = sum_k q16 * (w - zp), produced

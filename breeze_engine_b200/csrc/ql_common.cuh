@@ -36,6 +36,7 @@ enum : int {
     QL_ETIMEOUT = 4,      // a bounded device wait gave up (device error word)
     QL_EDEVICE = 5,       // handle lives on a different device than requested
     QL_ENOTSUP = 6,       // unsupported configuration
+    QL_ESCRATCH = 7,      // request needs more than the fixed scratch of the no-alloc entry point
 };
 
 // ---------------------------------------------------------------- device error word

@@ -73,6 +73,10 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 
+// Size of the fixed scratch behind ql_matmul_dev_noalloc (ql_api.cu); the
+// public header states the same value as QL_NOALLOC_SCRATCH_BYTES.
+constexpr size_t QL_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;
+
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
                                 const ActView& out, cudaStream_t stream);

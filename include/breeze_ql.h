@@ -38,8 +38,12 @@ enum {
     QL_ECUDA = 3,     /* CUDA runtime error (see ql_last_cuda_error_string) */
     QL_ETIMEOUT = 4,  /* a bounded device wait gave up                 */
     QL_EDEVICE = 5,   /* handle belongs to another device              */
-    QL_ENOTSUP = 6    /* unsupported configuration                     */
+    QL_ENOTSUP = 6,   /* unsupported configuration                     */
+    QL_ESCRATCH = 7   /* request exceeds the fixed scratch of ql_matmul_dev_noalloc */
 };
+
+/* Bytes of the fixed device scratch behind ql_matmul_dev_noalloc. */
+#define QL_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /* ---------------------------------------------------------------- group 1 */
 
@@ -135,6 +139,21 @@ int ql_quantize_act_dev(const float* dA, int M, int K, int hi_prec, void* ws, si
                         void* stream);
 int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, float* dC,
                             void* stream);
+
+/* ql_matmul_dev without any device allocation (no counterpart in the
+ * reference, which allocates its activation scratch on every call,
+ * kernel/quantized_matmul.cpp:532-534).  For callers that cannot allocate
+ * device memory when they run a layer: code being captured into a CUDA graph
+ * (cudaMalloc is not allowed during capture), serving runtimes whose allocator
+ * owns all of HBM, and per-token loops that cannot pay for an allocation or the
+ * synchronisation a free implies.  The quantized activations live in a fixed
+ * QL_NOALLOC_SCRATCH_BYTES array compiled into the library, held by every GPU
+ * that loads it until exit; requests that need more (ql_workspace_bytes(handle,
+ * M) larger than that) return QL_ESCRATCH.  The first call on a device looks up
+ * the array's device address (make it before any stream capture).  All calls
+ * share the array: calls whose work overlaps on the GPU race, so serialise them.
+ * Same numerics and arguments as ql_matmul_dev. */
+int ql_matmul_dev_noalloc(void* handle, const float* dA, int M, float* dC, void* stream);
 
 /* The per-block INT32 accumulators cs[M][N][K/32] = sum_k q16*(w-zp) of the
  * reference's tile_kernel (kernel/quantized_matmul.cpp:298-312, 262-268),
