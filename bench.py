@@ -233,14 +233,16 @@ def run_ours(args):
 
     stream = torch.cuda.current_stream()
 
-    def timed_replays(g, n):
+    def timed_replays(g, n, label="bench"):
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(label)          # lets ncu --nvtx restrict a capture to it
         e0.record(stream)
         for _ in range(n):
             g.replay()
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
         return max_over_ranks(e0.elapsed_time(e1) / 1e3)
@@ -255,7 +257,7 @@ def run_ours(args):
     t_probe = timed_replays(graph, 5) / 5
     n_window = max(1, int(1.0 / max(t_probe, 1e-6)))
     timed_replays(graph, n_window)
-    t = timed_replays(graph, args.steps)
+    t = timed_replays(graph, args.steps, label="timed")
     clock_info = clocks.stop()
     clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
 
@@ -296,11 +298,15 @@ def run_ours(args):
         del gk
     peak, peak_kind = measured_peaks()
     achieved = kern_b / kern_t / 1e9
+    # DRAM traffic from the committed ncu capture of one decode launch
+    # (profiles/decode_traffic.json: dram bytes read+write and the algorithmic
+    # bytes of that launch), scaled to this sweep's average launch.
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get("bytes_per_launch")
+            tr = json.load(open(tpath))
+            traffic = round(tr["dram_bytes"] / tr["alg_bytes"] * kern_b / len(calls))
         except Exception:  # noqa: BLE001
             traffic = None
 
@@ -485,6 +491,31 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_ncu_case(K, N, bits, M, launches=4):
+    """One layer (N(0, 0.02) weights, RTN-packed; INT8 per channel), activations
+    quantized once (two-pass), then `launches` decode-kernel launches rotating
+    over enough weight copies that each launch streams from HBM."""
+    import torch
+    from breeze_engine_b200 import _lib as L
+    lib = L.load()
+    torch.cuda.set_device(0)
+    copies = int(max(1, min(4, -(-2 * L2_BYTES // (N * K * bits // 8)))))
+    layer = Layer(lib, K, N, bits, 1, 0, 1234, copies)
+    a = torch.randn((M, K), device="cuda", dtype=torch.float32)
+    n = lib.ql_act_workspace_bytes(M, K)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    c = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.ql_quantize_act_dev(a.data_ptr(), M, K, 1, ws.data_ptr(), n, s) == 0
+    for i in range(launches):
+        h = layer.handles[i % len(layer.handles)]
+        assert lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    layer.free()
+    print(json.dumps({"ncu_case": [K, N, bits, M], "launches": launches, "copies": copies,
+                      "alg_bytes_per_launch": decode_kernel_bytes(M, K, N, bits)}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -493,10 +524,15 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", metavar="K,N,BITS,M", default=None,
+                    help="profiling driver: pack one layer, quantize once, run the decode kernel "
+                         "4 times and exit (for ncu captures of a single launch)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.ncu_case:
+        run_ncu_case(*map(int, args.ncu_case.split(",")))
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
