@@ -1,0 +1,84 @@
+"""Column/row-parallel quantized linear on 2 GPUs (NCCL), one process per GPU.
+
+Skipped when fewer than 2 GPUs are visible.  Column-parallel outputs must be
+bit-identical to the 1-GPU oracle result; row-parallel outputs agree within
+1e-5 relative per row (FP32 partials are summed across ranks).
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:  # noqa: BLE001
+        return 0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from breeze_engine_b200 import backend, sharded
+        from oracle.oracle import Oracle
+        backend.set_hi_prec(True)
+        rng = np.random.default_rng(11)
+        N, K, bits = 256, 32 * 12, 4
+        nblk = K // 32
+        qw = rng.integers(0, 256, (N, nblk, 16), dtype=np.uint8)
+        sc = rng.uniform(1e-3, 2e-2, (N, nblk)).astype(np.float16)
+        qz = rng.integers(0, 256, (N, (nblk + 1) // 2), dtype=np.uint8)
+        out = {}
+        for M in (1, 37):
+            a = rng.standard_normal((M, K)).astype(np.float32)
+            full = Oracle().matmul(qw, sc, qz, N, K, bits, a)
+            at = torch.from_numpy(a).cuda()
+            col = sharded.ColumnParallelLinear(qw, sc, qz, K, N, bits)
+            got = col(at).cpu().numpy()
+            out[f"col{M}"] = bool(np.array_equal(got.view(np.uint32), full.view(np.uint32)))
+            col.close()
+            row = sharded.RowParallelLinear(qw, sc, qz, K, N, bits)
+            got = row(at).cpu().numpy()
+            out[f"row{M}"] = float((np.abs(got - full).max(axis=1) / np.abs(full).max(axis=1)).max())
+            row.close()
+        torch.cuda.synchronize()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_column_and_row_parallel_on_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, out in results.items():
+        assert out["col1"] and out["col37"], (rank, out)
+        assert out["row1"] <= 1e-5 and out["row37"] <= 1e-5, (rank, out)
