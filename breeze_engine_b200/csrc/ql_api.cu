@@ -8,6 +8,7 @@
 // The ql_* entry points take device pointers and a cudaStream_t (as void*),
 // enqueue asynchronously and return an int status (0 = OK).
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -131,11 +132,22 @@ cudaStream_t internal_stream(DeviceState* st) {
     return st->stream;
 }
 
-// Workspace for M tokens of K inputs: one activation chunk per 64 tokens,
-// each laid out by act_carve (the quantized planes and scales of that chunk).
+// M > 64 tokens run the tcgen05 GEMM (ql_gemm.cu) unless BREEZE_QL_PREFILL=decode
+// asks for the decode kernel over 64-token chunks (kept for comparison).
+bool use_gemm(int M) {
+    static const int force_decode = [] {
+        const char* v = std::getenv("BREEZE_QL_PREFILL");
+        return (v && std::strcmp(v, "decode") == 0) ? 1 : 0;
+    }();
+    return M > MAX_DECODE_TOKENS && !force_decode;
+}
+
+// Workspace for M tokens of K inputs: GEMM activation records for the tcgen05
+// path, else one decode activation chunk per 64 tokens laid out by act_carve.
 size_t chunk_bytes(int M, int nblk) { return act_bytes(std::min(M, MAX_DECODE_TOKENS), nblk); }
 size_t ws_bytes_for(int M, int nblk) {
     if (M <= 0) return 0;
+    if (use_gemm(M)) return gemm_act_bytes(M, nblk);
     const size_t chunks = static_cast<size_t>((M + MAX_DECODE_TOKENS - 1) / MAX_DECODE_TOKENS);
     return chunks * chunk_bytes(M, nblk);
 }
@@ -148,6 +160,8 @@ ActView chunk_view(void* ws, int M, int nblk, int c, bool hi_prec) {
 
 int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, bool hi_prec) {
     const int nblk = K / 32;
+    if (use_gemm(M))
+        return cuda_status(launch_quantize_gemm(dA, K, M, K, hi_prec, static_cast<uint8_t*>(ws), stream));
     for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
         const ActView act = chunk_view(ws, M, nblk, c, hi_prec);
         cudaError_t e = launch_quantize_act(dA + static_cast<size_t>(c) * MAX_DECODE_TOKENS * K, K,
@@ -159,6 +173,8 @@ int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, b
 
 int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS, cudaStream_t stream,
                 bool hi_prec, bool pdl) {
+    if (use_gemm(M))
+        return cuda_status(launch_gemm(w, static_cast<const uint8_t*>(ws), M, hi_prec, dC, w->N, dCS, stream));
     for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
         const ActView act = chunk_view(const_cast<void*>(ws), M, w->nblk, c, hi_prec);
         const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
@@ -174,7 +190,8 @@ int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS,
 // the quantizer finishes.
 int run_matmul(const Weight* w, const float* dA, int M, float* dC, int32_t* dCS, void* ws,
                size_t ws_bytes, cudaStream_t stream, bool hi_prec) {
-    if (ws_bytes < ws_bytes_for(M, w->nblk)) return set_status(QL_EINVAL);
+    if (ws_bytes < ws_bytes_for(M, w->nblk) || reinterpret_cast<uintptr_t>(ws) % 16)
+        return set_status(QL_EINVAL);        // bulk copies read the workspace in 16-byte units
     if (M <= MAX_DECODE_TOKENS) {
         int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
         if (rc != QL_OK) return rc;
@@ -483,18 +500,21 @@ QL_API int ql_quantize_act_dev(const float* dA, int M, int K, int hi_prec, void*
                                void* stream) {
     if (M < 0 || K <= 0 || K % 32) return set_status(QL_EINVAL);
     if (M == 0) return set_status(QL_OK);
-    if (!dA || !ws || reinterpret_cast<uintptr_t>(dA) % 16 || ws_bytes < ws_bytes_for(M, K / 32))
+    if (!dA || !ws || reinterpret_cast<uintptr_t>(dA) % 16 || reinterpret_cast<uintptr_t>(ws) % 16 ||
+        ws_bytes < ws_bytes_for(M, K / 32))
         return set_status(QL_EINVAL);
     return run_quantize(dA, M, K, ws, static_cast<cudaStream_t>(stream), hi_prec != 0);
 }
 
 // C[M,N] from activations quantized by ql_quantize_act_dev with the same M, K
-// and hi_prec.  Streams the packed weights once per 64-token chunk.
+// and hi_prec.  Up to 64 tokens stream the packed weights once per call; more
+// tokens run the tensor-core GEMM (or, with BREEZE_QL_PREFILL=decode, stream
+// them once per 64-token chunk).
 QL_API int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, float* dC,
                                    void* stream) {
     if (!valid_weight(handle) || M < 0) return set_status(QL_EINVAL);
     if (M == 0) return set_status(QL_OK);
-    if (!ws || !dC) return set_status(QL_EINVAL);
+    if (!ws || !dC || reinterpret_cast<uintptr_t>(ws) % 16) return set_status(QL_EINVAL);
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return set_status(QL_ECUDA);
     const auto* w = static_cast<const Weight*>(handle);

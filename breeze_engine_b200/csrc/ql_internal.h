@@ -73,6 +73,16 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 
+// Prefill (M > MAX_DECODE_TOKENS) runs the tcgen05 GEMM (ql_gemm.cu) on
+// activations quantized into GEMM records: per (128-token tile, block) the hi
+// and lo planes as canonical K-major tcgen05 B operands, then 128 fp32 scales.
+constexpr int GEMM_AREC = 4096 + 4096 + 128 * 4;
+size_t gemm_act_bytes(int M, int nblk);
+cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
+                                 cudaStream_t stream);
+cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec, float* C, int ldc,
+                        int32_t* cs, cudaStream_t stream);
+
 // Size of the fixed scratch behind ql_matmul_dev_noalloc (ql_api.cu); the
 // public header states the same value as QL_NOALLOC_SCRATCH_BYTES.
 constexpr size_t QL_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;

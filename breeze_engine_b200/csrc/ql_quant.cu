@@ -103,6 +103,89 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     }
 }
 
+// GEMM-layout variant (M > 64, ql_gemm.cu): one record of GEMM_AREC bytes per
+// (128-token tile, block): the hi plane (hi - 128, s8) and the lo plane (u8;
+// q8 in single-pass mode) as canonical K-major tcgen05 B operands
+// [2 K halves][16 groups of 8 tokens][8 tokens x 16 B], then 128 fp32 scales.
+// Tokens M..(tile end) are written as zeros.
+template <bool HP>
+__global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restrict__ A, int lda, int M, int K,
+                                                            int m_tiles, uint8_t* __restrict__ out) {
+    pdl_launch_dependents();
+    const int nblk = K / BLOCK_K;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(m_tiles) * 128 * nblk) return;
+    const int m = static_cast<int>(idx / nblk);
+    const int b = static_cast<int>(idx % nblk);
+    const int mt = m >> 7, mr = m & 127;
+    uint8_t* rec = out + (static_cast<size_t>(mt) * nblk + b) * GEMM_AREC;
+    const int o = (mr >> 3) * 128 + (mr & 7) * 16;            // K half 0; K half 1 at +2048
+    float* scales = reinterpret_cast<float*>(rec + 8192);
+    if (m >= M) {
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(rec + o) = z;
+        *reinterpret_cast<uint4*>(rec + o + 2048) = z;
+        *reinterpret_cast<uint4*>(rec + 4096 + o) = z;
+        *reinterpret_cast<uint4*>(rec + 4096 + o + 2048) = z;
+        scales[mr] = 0.0f;
+        return;
+    }
+    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = __ldg(src + i);
+        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float a = fabsf(v[i]);
+        amax = (a > amax) ? a : amax;
+    }
+    constexpr float QMAX = HP ? 32767.0f : 127.0f;
+    constexpr int IMAX = HP ? 32767 : 127;
+    const float scale = __fdiv_rn(amax, QMAX);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    scales[mr] = scale;
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t hword = 0, lword = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int q = to_int_like_lrint(__fmul_rn(v[4 * w + j], inv));
+            q = q > IMAX ? IMAX : (q < -IMAX ? -IMAX : q);
+            if (HP) {
+                const uint32_t u = static_cast<uint32_t>(q + 32768);
+                hword |= ((u >> 8) ^ 0x80u) << (8 * j);
+                lword |= (u & 0xFFu) << (8 * j);
+            } else {
+                lword |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+            }
+        }
+        hw[w] = hword;
+        lw[w] = lword;
+    }
+    *reinterpret_cast<uint4*>(rec + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(rec + o + 2048) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    *reinterpret_cast<uint4*>(rec + 4096 + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4*>(rec + 4096 + o + 2048) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+}
+
+cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
+                                 cudaStream_t stream) {
+    const int m_tiles = (M + 127) / 128;
+    const long long total = static_cast<long long>(m_tiles) * 128 * (K / BLOCK_K);
+    const int threads = 256;
+    const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+    if (hi_prec)
+        quantize_gemm_kernel<true><<<grid, threads, 0, stream>>>(A, lda, M, K, m_tiles, out);
+    else
+        quantize_gemm_kernel<false><<<grid, threads, 0, stream>>>(A, lda, M, K, m_tiles, out);
+    return cudaGetLastError();
+}
+
 // Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
 // reference's au8_hi / au8_lo) and ascale [M][K/32].
 __global__ void __launch_bounds__(256) quantize_ref_kernel(const float* __restrict__ A, int M, int K,
