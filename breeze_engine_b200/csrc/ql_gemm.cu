@@ -49,15 +49,9 @@ constexpr int NEPI = 8;                // epilogue warps: 4 TMEM lane quarters x
 constexpr int NWARPS = 4 + NEPI;
 constexpr int ECOLS = TILE_M / (NEPI / 4);   // token columns per epilogue thread (64)
 constexpr int ECH = ECOLS / 8;               // 8-column TMEM chunks per block (block-sum path)
-constexpr int ECW = 32;                      // TMEM columns per epilogue load (fast path)
 constexpr int A_SLOT = TILE_N * 32;    // canonical s8 weight tile per block (4 KB)
 constexpr int NA = 4;                  // canonical weight slots
 constexpr uint32_t TMEM_COLS = 512;    // two accumulator slots of hi|lo x 128 columns
-constexpr int REGS_LAUNCH = 168;       // registers per thread at launch (384 threads, 1 CTA per SM)
-constexpr int REGS_CTRL = 56;          // producer, MMA and unpack warps after setmaxnreg.dec
-constexpr int REGS_EPI = 224;          // epilogue warps after setmaxnreg.inc
-static_assert(4 * 32 * REGS_CTRL + NEPI * 32 * REGS_EPI == NWARPS * 32 * REGS_LAUNCH,
-              "register split must equal the launch allocation");
 
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     uint64_t d = 0;
@@ -94,34 +88,11 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                 : "r"(taddr));
-}
-__device__ __forceinline__ __attribute__((unused)) void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                   "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                   "=r"(r[14]), "=r"(r[15])
-                 : "r"(taddr));
-}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Writes the 32-bit value v to 8 consecutive columns of the warp's 32 lanes.
 __device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t v) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "r"(taddr), "r"(v) : "memory");
-}
-template <int W> __device__ __forceinline__ void tmem_ld(uint32_t a, uint32_t (&r)[W]) {
-    static_assert(W == 16 || W == 32, "TMEM load width");
-    if constexpr (W == 16) tmem_ld16(a, r);
-    else tmem_ld32(a, r);
 }
 // Shared-memory float4 load kept in program order (volatile), so the
 // compiler cannot hoist a whole block's activation scales into registers.
@@ -246,12 +217,7 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
     __syncthreads();
     tc_fence_after();
 
-    // Register split (setmaxnreg): the producer / MMA / unpack warpgroup needs few
-    // registers and hands them to the two epilogue warpgroups.  Launched with
-    // REGS_LAUNCH per thread (the host checks), 128 x REGS_CTRL + 256 x REGS_EPI
-    // equals the block's 384 x REGS_LAUNCH, so every increase can be granted.
     if (warp < 4) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(REGS_CTRL));
         if (warp == 0) {
             // ------------------------------------------------------------ producer
             // The whole warp runs the loop and waits (it stays converged); lane 0
@@ -388,7 +354,6 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
             }
         }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(REGS_EPI));
         // ------------------------------------------------------------ epilogue
         const int e = warp - 4;
         const int q = warp & 3;                           // TMEM lane quarter (hardware rule: warp % 4)
@@ -444,37 +409,41 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
                             }
                         }
                     } else {
-                    // chunks of ECW token columns: load hi and lo, re-seed the
-                    // columns for this slot's next block, convert and rescale
+                    // 8-column chunks; the next chunk's TMEM loads are in flight while
+                    // this chunk is converted and rescaled, and each chunk's columns
+                    // are re-seeded for the slot's next block right after they are read
+                    uint32_t hv[2][8], lv[2][8];
+                    if (HP) tmem_ld8(t_hi, hv[0]);
+                    tmem_ld8(t_hi + 128, lv[0]);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int ch = 0; ch < ECOLS / ECW; ++ch) {
-                        uint32_t hv[ECW], lv[ECW];
-                        if (HP) tmem_ld<ECW>(t_hi + ch * ECW, hv);
-                        tmem_ld<ECW>(t_hi + 128 + ch * ECW, lv);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int f = 0; f < ECW; f += 8) {      // x8 fills: one 8-register seed vector each
-                            if (HP) tmem_fill8(t_hi + ch * ECW + f, static_cast<uint32_t>(HI_SEED));
-                            tmem_fill8(t_hi + 128 + ch * ECW + f, static_cast<uint32_t>(LO_SEED));
+                    for (int cc = 0; cc < ECH; ++cc) {
+                        const int cur = cc & 1;
+                        if (cc < ECH - 1) {
+                            if (HP) tmem_ld8(t_hi + (cc + 1) * 8, hv[cur ^ 1]);
+                            tmem_ld8(t_hi + 128 + (cc + 1) * 8, lv[cur ^ 1]);
                         }
+                        if (HP) tmem_fill8(t_hi + cc * 8, static_cast<uint32_t>(HI_SEED));
+                        tmem_fill8(t_hi + 128 + cc * 8, static_cast<uint32_t>(LO_SEED));
 #pragma unroll
-                        for (int k = 0; k < ECW; k += 4) {
-                            const float4 a4 = lds_f4(ascale + ch * ECW + k);
+                        for (int k = 0; k < 8; k += 4) {
+                            const float4 a4 = lds_f4(ascale + cc * 8 + k);
                             uint64_t y0, y1;
                             if (HP) {
-                                y0 = cs_to_f2(static_cast<int32_t>(hv[k]), static_cast<int32_t>(hv[k + 1]),
-                                              static_cast<int32_t>(lv[k]), static_cast<int32_t>(lv[k + 1]));
-                                y1 = cs_to_f2(static_cast<int32_t>(hv[k + 2]), static_cast<int32_t>(hv[k + 3]),
-                                              static_cast<int32_t>(lv[k + 2]), static_cast<int32_t>(lv[k + 3]));
+                                y0 = cs_to_f2(static_cast<int32_t>(hv[cur][k]), static_cast<int32_t>(hv[cur][k + 1]),
+                                              static_cast<int32_t>(lv[cur][k]), static_cast<int32_t>(lv[cur][k + 1]));
+                                y1 = cs_to_f2(static_cast<int32_t>(hv[cur][k + 2]), static_cast<int32_t>(hv[cur][k + 3]),
+                                              static_cast<int32_t>(lv[cur][k + 2]), static_cast<int32_t>(lv[cur][k + 3]));
                             } else {
                                 const uint64_t neg = f2_pack(-12582912.0f, -12582912.0f);   // -1.5*2^23
-                                y0 = f2_add(i2_pack(static_cast<int32_t>(lv[k]), static_cast<int32_t>(lv[k + 1])), neg);
-                                y1 = f2_add(i2_pack(static_cast<int32_t>(lv[k + 2]), static_cast<int32_t>(lv[k + 3])), neg);
+                                y0 = f2_add(i2_pack(static_cast<int32_t>(lv[cur][k]), static_cast<int32_t>(lv[cur][k + 1])), neg);
+                                y1 = f2_add(i2_pack(static_cast<int32_t>(lv[cur][k + 2]), static_cast<int32_t>(lv[cur][k + 3])), neg);
                             }
-                            const int i0 = (ch * ECW + k) >> 1;
+                            const int i0 = (cc * 8 + k) >> 1;
                             acc[i0] = f2_fma(f2_pack(a4.x, a4.y), f2_mul(y0, bs2), acc[i0]);
                             acc[i0 + 1] = f2_fma(f2_pack(a4.z, a4.w), f2_mul(y1, bs2), acc[i0 + 1]);
                         }
+                        if (cc < ECH - 1) tmem_wait_ld();
                     }
                     }
                     // the slot is read and re-seeded: hand it back to the MMA warp
@@ -534,13 +503,7 @@ static cudaError_t gemm_launch(const GemmParams& p0, cudaStream_t stream) {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!configured[dev]) {
-        // The setmaxnreg split assumes exactly REGS_LAUNCH registers per thread
-        // at launch; with fewer, an increase could never be granted.
-        cudaFuncAttributes fa = {};
-        cudaError_t e = cudaFuncGetAttributes(&fa, kern);
-        if (e != cudaSuccess) return e;
-        if (fa.numRegs != REGS_LAUNCH) return cudaErrorInvalidConfiguration;
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
