@@ -1,25 +1,33 @@
 #!/usr/bin/env python
 """Benchmark of the B200 quantized-linear hot path (one JSON line on rank 0).
 
-Workload (default ``--workload decode``): the INT8
-decode GEMV sweep -- batch M in {1, 4, 8, 16} x (K, N) in {(4096, 12288),
-(12288, 4096), (4096, 151936)}, weights N(0, 0.02) packed to INT8 per output
-channel, activations N(0, 1) quantized to two-pass INT16.  One *step* is the
-12 calls of the sweep.  ``value`` is the whole-job HBM throughput:
-algorithmic bytes of the 12 calls (``N*K*bits/8 + 2*N*K/32 + 4*M*K + 4*M*N``
-each) / device time of the step, max over ranks.  With ``--gpus P`` every layer
-is column-parallel (N/P per GPU) and the output shards are NCCL-all-gathered:
-total work is fixed, so scaling is "strong".
+Workloads (``--workload``):
 
+* ``decode`` (default): the INT8 decode GEMV sweep --
+  batch M in {1, 4, 8, 16} x (K, N) in {(4096, 12288), (12288, 4096),
+  (4096, 151936)}, weights N(0, 0.02) packed to INT8 per output channel,
+  activations N(0, 1) quantized to two-pass INT16.  One *step* is the 12 calls
+  of the sweep.  ``value`` is the whole-job HBM throughput: algorithmic bytes of
+  the 12 calls (``N*K*bits/8 + 2*N*K/32 + 4*M*K + 4*M*N`` each) / device time
+  of the step, max over ranks.
+* ``prefill``: the INT4 prefill GEMM -- M in {128, 512, 2048}
+  tokens, K = 5120, N = 17408, weights N(0, 0.02) RTN-packed to INT4 with fp16
+  scales, activations N(0, 1) with 1% of the channels scaled x20 (outliers),
+  two-pass INT16.  One step is the 3 calls.  ``value`` is INT8 tera-operations
+  per second counted as BASELINE.md does: ``4*M*N*K`` per call (two INT8
+  passes of 2*M*N*K each).
+
+With ``--gpus P`` every layer is column-parallel (N/P per GPU) and the output
+shards are NCCL-all-gathered: total work is fixed, so scaling is "strong".
 Other BASELINE configs are parity-test cases (tests/), not bench lines.
 
 Inputs stay resident in HBM; every call streams its weights from HBM because
-each small layer is packed into several copies that are rotated (the working
-set of a step, > 1 GB, is far above the 126 MB L2).
+each layer is packed into several copies that are rotated (the working set of
+a step is far above the 126 MB L2).
 
 ``--impl reference`` times the reference's own VNNI/OpenMP ``i4_matmul``
 (oracle/_ref, built from kernel/quantized_matmul.cpp) on the host cores for the
-same sweep and metric; under torchrun only rank 0 runs it.
+same workload and metric; under torchrun only rank 0 runs it.
 """
 import argparse
 import ctypes
@@ -36,14 +44,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-DECODE_SHAPES = [(4096, 12288), (12288, 4096), (4096, 151936)]   # (K, N)
-DECODE_M = [1, 4, 8, 16]
-PREFILL = dict(K=5120, N=17408, Ms=[128, 512, 2048])
-LAYER = [("q", 5120, 6144), ("k", 5120, 1024), ("v", 5120, 1024), ("o", 6144, 5120),
-         ("gate", 5120, 17408), ("up", 5120, 17408), ("down", 17408, 5120)]
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-METRIC = "decode GEMV HBM throughput (INT8 weights, two-pass INT16 activations)"
+NOMINAL_INT8_TOPS = 4500.0           # dense INT8, B200 (NVIDIA's figure without sparsity)
+SMS = 148
 
 
 def alg_bytes(M, K, N, bits):
@@ -55,6 +59,11 @@ def decode_kernel_bytes(M, K, N, bits):
     """Algorithmic bytes of the weight-streaming kernel alone: packed weights,
     fp16 scales, the two INT8 activation planes and their scales, FP32 output."""
     return N * K * bits // 8 + 2 * N * (K // 32) + 2 * M * K + 4 * M * (K // 32) + 4 * M * N
+
+
+def prefill_ops(M, K, N):
+    """Algorithmic INT8 operations of one call: two INT8 passes of 2*M*N*K."""
+    return 4 * M * N * K
 
 
 # ------------------------------------------------------------------ helpers
@@ -72,6 +81,32 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:  # noqa: BLE001
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measure_int8_tops(n=8192, iters=10):
+    """Dense INT8 tensor-core peak of this GPU, measured now: cuBLASLt INT8
+    GEMM (torch._int_mm, int32 output) on n^3, best of `iters` CUDA-event runs."""
+    import torch
+    try:
+        a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) / 1e3
+            best = t if best is None else min(best, t)
+        del a, b
+        torch.cuda.empty_cache()
+        return 2.0 * n ** 3 / best / 1e12, f"measured: cuBLASLt INT8 GEMM (torch._int_mm) {n}^3, best of {iters}"
+    except Exception as exc:  # noqa: BLE001
+        return NOMINAL_INT8_TOPS, f"nominal dense INT8 (measurement failed: {type(exc).__name__})"
 
 
 class ClockSampler:
@@ -124,7 +159,6 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-# ------------------------------------------------------------------ our arm
 
 class Layer:
     """One packed weight (possibly several rotation copies) of a (K, N) layer shard."""
@@ -154,25 +188,140 @@ class Layer:
             backend.free(h)
 
 
-def build_decode(lib, world, rank):
-    import torch
-    layers = []
-    for i, (K, N) in enumerate(DECODE_SHAPES):
-        shard = (N // world) * K + 2 * (N // world) * (K // 32)
-        copies = int(min(len(DECODE_M), max(1, -(-2 * L2_BYTES // shard))))
-        layers.append(Layer(lib, K, N, 8, world, rank, 1000 + i, copies))
-    g = torch.Generator(device="cuda")
-    g.manual_seed(7)
-    acts = {}
-    for K in sorted({k for k, _ in DECODE_SHAPES}):
-        for M in DECODE_M:
-            acts[(M, K)] = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
-    calls = []
-    for layer in layers:
-        for j, M in enumerate(DECODE_M):
-            calls.append((layer, layer.handles[j % len(layer.handles)], M))
-    return layers, acts, calls
 
+# ------------------------------------------------------------------ workloads
+
+def _outlier_acts(M, K, seed):
+    """N(0, 1) activations with 1% of the channels scaled x20 (the outlier
+    channels exercise the INT16 hi/lo split); seeded, on the device."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    a = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
+    ch = torch.randperm(K, generator=g, device="cuda")[: max(1, K // 100)]
+    a[:, ch] *= 20.0
+    return a
+
+
+class DecodeWorkload:
+    name = "decode"
+    metric = "decode GEMV HBM throughput (INT8 weights, two-pass INT16 activations)"
+    unit = "GB/s"
+    shapes = [(4096, 12288), (12288, 4096), (4096, 151936)]   # (K, N)
+    Ms = [1, 4, 8, 16]
+    bits = 8
+    kernel = "decode_kernel (ql_gemv.cu)"
+
+    def build(self, lib, world, rank):
+        import torch
+        layers = []
+        for i, (K, N) in enumerate(self.shapes):
+            shard = (N // world) * K + 2 * (N // world) * (K // 32)
+            copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
+            layers.append(Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies))
+        g = torch.Generator(device="cuda")
+        g.manual_seed(7)
+        acts = {}
+        for K in sorted({k for k, _ in self.shapes}):
+            for M in self.Ms:
+                acts[(M, K)] = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
+        calls = []
+        for layer in layers:
+            for j, M in enumerate(self.Ms):
+                calls.append((layer, layer.handles[j % len(layer.handles)], M))
+        return layers, acts, calls
+
+    def step_amount(self, calls):
+        return sum(alg_bytes(M, layer.K, layer.N, layer.bits) for layer, _, M in calls)
+
+    def value(self, amount, seconds):
+        return amount / seconds / 1e9
+
+    def kernel_amount(self, M, K, n_local, bits):
+        return decode_kernel_bytes(M, K, n_local, bits)
+
+    def roofline(self, achieved, kern_amount_avg, calls, clock_mhz):
+        peak, kind = measured_peaks()
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
+        if os.path.exists(tpath):
+            try:
+                tr = json.load(open(tpath))
+                traffic = round(tr["dram_bytes"] / tr["alg_bytes"] * kern_amount_avg)
+            except Exception:  # noqa: BLE001
+                traffic = None
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic}
+
+    def config(self, world):
+        return {"workload": "configs[1]: INT8 decode GEMV sweep", "M": self.Ms,
+                "shapes_KN": self.shapes, "weights": "INT8 per-channel RTN, fp16 scales",
+                "activations": "two-pass INT16 (hi_prec=1)",
+                "l2": "rotated weight copies; step working set > L2",
+                "timing": "CUDA graph of one step (12 quantize+matmul calls), CUDA events",
+                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+
+    def cpu_calls(self):
+        """(K, N, bits, Ms) of the reference timing; `samples` steps of these."""
+        return [(K, N, self.bits, self.Ms) for K, N in self.shapes]
+
+    cpu_sample = "full decode sweeps (12 i4_matmul calls each)"
+
+
+class PrefillWorkload:
+    name = "prefill"
+    metric = "prefill GEMM INT8 TOPS (INT4 weights, two-pass INT16 activations; 4*M*N*K per call)"
+    unit = "TOPS"
+    K, N, Ms, bits = 5120, 17408, [128, 512, 2048], 4
+    kernel = "gemm_kernel (ql_gemm.cu, tcgen05 kind::i8)"
+
+    def build(self, lib, world, rank):
+        layer = Layer(lib, self.K, self.N, self.bits, world, rank, 3000, len(self.Ms))
+        acts = {(M, self.K): _outlier_acts(M, self.K, 11 + M) for M in self.Ms}
+        calls = [(layer, layer.handles[j % len(layer.handles)], M) for j, M in enumerate(self.Ms)]
+        return [layer], acts, calls
+
+    def step_amount(self, calls):
+        return sum(prefill_ops(M, layer.K, layer.N) for layer, _, M in calls)
+
+    def value(self, amount, seconds):
+        return amount / seconds / 1e12
+
+    def kernel_amount(self, M, K, n_local, bits):
+        return prefill_ops(M, K, n_local)
+
+    def roofline(self, achieved, kern_amount_avg, calls, clock_mhz):
+        peak, kind = measure_int8_tops()
+        out = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "peak_kind": kind,
+               "unit": "TFLOP/s (INT8 TOPS)", "frac": round(achieved / peak, 4), "traffic": None}
+        # The reference algorithm rescales every (token, column, block) in FP32:
+        # exact RN(256*S_hi + S_lo) (2 adds), *bscale, fma(ascale, ., acc): 4 FP32
+        # operations per output per 32-wide block on the 128-lane FP32 pipe.
+        if clock_mhz:
+            fp32_ops_s = SMS * 128 * clock_mhz * 1e6
+            ops_per_tops = 4.0 / (32 * 4)           # FP32 ops per counted INT8 op (4*M*N*K)
+            out["fp32_epilogue_bound_tops"] = round(fp32_ops_s / ops_per_tops / 1e12, 1)
+            out["fp32_epilogue_frac"] = round(achieved / out["fp32_epilogue_bound_tops"], 4)
+        return out
+
+    def config(self, world):
+        return {"workload": "configs[2]: INT4 prefill GEMM", "M": self.Ms, "K": self.K, "N": self.N,
+                "weights": "INT4 symmetric RTN, fp16 scales (block 32)",
+                "activations": "two-pass INT16 (hi_prec=1); N(0,1), 1% channels x20",
+                "l2": "3 rotated weight copies; step working set > L2",
+                "timing": "CUDA graph of one step (3 quantize+GEMM calls), CUDA events",
+                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+
+    def cpu_calls(self):
+        return [(self.K, self.N, self.bits, [128])]
+
+    cpu_sample = "i4_matmul calls at M=128 (the smallest prefill size)"
+
+
+WORKLOADS = {"decode": DecodeWorkload, "prefill": PrefillWorkload}
+
+
+# ------------------------------------------------------------------ our arm
 
 def run_ours(args):
     import torch
@@ -181,6 +330,7 @@ def run_ours(args):
     from breeze_engine_b200 import backend
     from breeze_engine_b200.sharded import gather_columns
 
+    wl = WORKLOADS[args.workload]()
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
     if world > 1:
@@ -190,7 +340,7 @@ def run_ours(args):
     lib = L.load()
     backend.set_hi_prec(True)
 
-    layers, acts, calls = build_decode(lib, world, rank)
+    layers, acts, calls = wl.build(lib, world, rank)
     outs, wss = {}, {}
     for layer, h, M in calls:
         outs[(id(layer), M)] = torch.empty((M, layer.n_local), dtype=torch.float32, device="cuda")
@@ -254,19 +404,19 @@ def run_ours(args):
     # then take the timed region right after it.
     clocks = ClockSampler(local_rank)
     clocks.start()
-    t_probe = timed_replays(graph, 5) / 5
+    t_probe = timed_replays(graph, 3) / 3
     n_window = max(1, int(1.0 / max(t_probe, 1e-6)))
     timed_replays(graph, n_window)
     t = timed_replays(graph, args.steps, label="timed")
     clock_info = clocks.stop()
     clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
 
-    step_bytes = sum(alg_bytes(M, layer.K, layer.N, layer.bits) for layer, _, M in calls)
-    value = step_bytes * args.steps / t / 1e9
+    step_amount = wl.step_amount(calls)
+    value = wl.value(step_amount * args.steps, t)
 
-    # ---- per-launch pass (roofline): the weight-streaming kernel alone, on
-    # activations quantized once, REPS launches per call rotating over the
-    # layer's weight copies, captured in a graph and timed with CUDA events.
+    # ---- per-launch pass (roofline): the matmul kernel alone, on activations
+    # quantized once, REPS launches per call rotating over the layer's weight
+    # copies, captured in a graph and timed with CUDA events.
     qws = {}
     for layer, h, M in calls:
         key = (M, layer.K)
@@ -277,8 +427,8 @@ def run_ours(args):
                                          stream.cuda_stream)
             assert rc == 0
     torch.cuda.synchronize()
-    REPS = 8
-    kern_t, kern_b, per_call = 0.0, 0, []
+    REPS = 8 if wl.name == "decode" else 4
+    kern_t, kern_amount, per_call = 0.0, 0, []
     for layer, h0, M in calls:
         c, ws = outs[(id(layer), M)], qws[(M, layer.K)]
         gk = torch.cuda.CUDAGraph()
@@ -289,26 +439,18 @@ def run_ours(args):
                 rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s_ptr)
                 assert rc == 0
         gk.replay()
-        dt = timed_replays(gk, max(2, args.steps // 2)) / (max(2, args.steps // 2) * REPS)
-        b = decode_kernel_bytes(M, layer.K, layer.n_local, layer.bits)
+        nrep = max(2, args.steps // 2)
+        dt = timed_replays(gk, nrep) / (nrep * REPS)
+        amt = wl.kernel_amount(M, layer.K, layer.n_local, layer.bits)
         kern_t += dt
-        kern_b += b
+        kern_amount += amt
         per_call.append({"M": M, "K": layer.K, "N": layer.N, "us": round(dt * 1e6, 2),
-                         "GBps": round(b / dt / 1e9, 1)})
+                         wl.unit: round(wl.value(amt, dt), 1)})
         del gk
-    peak, peak_kind = measured_peaks()
-    achieved = kern_b / kern_t / 1e9
-    # DRAM traffic from the committed ncu capture of one decode launch
-    # (profiles/decode_traffic.json: dram bytes read+write and the algorithmic
-    # bytes of that launch), scaled to this sweep's average launch.
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            tr = json.load(open(tpath))
-            traffic = round(tr["dram_bytes"] / tr["alg_bytes"] * kern_b / len(calls))
-        except Exception:  # noqa: BLE001
-            traffic = None
+    achieved = wl.value(kern_amount, kern_t)
+    roofline = wl.roofline(achieved, kern_amount / len(calls), calls, clock_info.get("sm_mhz"))
+    roofline["kernel"] = wl.kernel
+    roofline["per_call"] = per_call
 
     # ---- end to end through the reference-compatible host C ABI (i4_matmul)
     e2e = None
@@ -330,7 +472,7 @@ def run_ours(args):
         for _ in range(args.steps):
             e2e_step()
         t_e2e = max_over_ranks(time.perf_counter() - t0)
-        e2e = {"value": round(step_bytes * args.steps / t_e2e / 1e9, 2), "unit": "GB/s",
+        e2e = {"value": round(wl.value(step_amount * args.steps, t_e2e), 2), "unit": wl.unit,
                "h2d_bytes_per_step": int(sum(4 * M * layer.K for layer, _, M in calls)),
                "d2h_bytes_per_step": int(sum(4 * M * layer.n_local for layer, _, M in calls)),
                "api": "i4_matmul (host pointers, pinned buffers, synchronous)"
@@ -338,24 +480,17 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(samples=2)
+        cpu = cpu_baseline(wl, samples=2)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "s8xs8/u8->s32, f32 rescale", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": "configs[1]: INT8 decode GEMV sweep", "M": DECODE_M,
-                       "shapes_KN": DECODE_SHAPES, "weights": "INT8 per-channel RTN, fp16 scales",
-                       "activations": "two-pass INT16 (hi_prec=1)",
-                       "l2": "rotated weight copies; step working set > L2",
-                       "timing": "CUDA graph of one step (12 quantize+matmul calls), CUDA events",
-                       "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": "decode_kernel (ql_gemv.cu)",
-                         "per_call": per_call},
+            "dtype": "s8xs8/u8->s32, f32 rescale",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": wl.config(world),
+            "roofline": roofline,
             "gpu_launches": 2 * len(calls) * args.steps,
             "clocks": clock_info,
         }
@@ -400,50 +535,66 @@ def _reference_lib():
     return Reference(), None
 
 
-def cpu_baseline(samples=2, shapes=None):
-    """Reference i4_matmul (OpenMP, all host threads) over the decode sweep."""
+class _RefCalls:
+    """The reference's i4_matmul over a list of (K, N, bits, Ms), host buffers."""
+
+    def __init__(self, ref, spec, threads):
+        self.ref = ref
+        self.handles = []
+        for i, (K, N, bits, Ms) in enumerate(spec):
+            qw, sc = host_weights(K, N, bits, 100 + i)
+            self.handles.append((K, N, bits, Ms, ref.prepack(qw, sc, None, K, N, bits)))
+            del qw
+        rng = np.random.default_rng(7)
+        self.acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32)
+                     for K, _, _, Ms in spec for M in Ms}
+        self.outs = {(M, N): np.empty((M, N), np.float32) for _, N, _, Ms in spec for M in Ms}
+        ref.lib.i4_set_threads(threads)
+        ref.lib.i4_set_hi_prec(1)
+
+    def step(self):
+        for K, N, _, Ms, h in self.handles:
+            for M in Ms:
+                self.ref.lib.i4_matmul(ctypes.c_void_p(h), self.acts[(M, K)].ctypes.data, M,
+                                       self.outs[(M, N)].ctypes.data)
+
+    def amount(self, wl):
+        if wl.name == "decode":
+            return sum(alg_bytes(M, K, N, bits) for K, N, bits, Ms, _ in self.handles for M in Ms)
+        return sum(prefill_ops(M, K, N) for K, N, _, Ms, _ in self.handles for M in Ms)
+
+    def free(self):
+        for *_, h in self.handles:
+            self.ref.free(h)
+
+
+def cpu_baseline(wl, samples=2):
+    """The reference i4_matmul (OpenMP, all host threads) on a bounded sample."""
     os.environ.setdefault("OMP_PROC_BIND", "spread")
     os.environ.setdefault("OMP_PLACES", "cores")
     ref, why = _reference_lib()
     if ref is None:
-        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": why}
+        return {"value": None, "unit": wl.unit, "cores": 0, "kind": "reference", "sample": why}
     threads = os.cpu_count() or 1
-    shapes = shapes or DECODE_SHAPES
-    handles = []
-    for i, (K, N) in enumerate(shapes):
-        qw, sc = host_weights(K, N, 8, 100 + i)
-        handles.append((K, N, ref.prepack(qw, sc, None, K, N, 8)))
-        del qw
-    rng = np.random.default_rng(7)
-    acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32) for K, _ in shapes for M in DECODE_M}
-    outs = {(M, N): np.empty((M, N), np.float32) for _, N in shapes for M in DECODE_M}
-    ref.lib.i4_set_threads(threads)
-    ref.lib.i4_set_hi_prec(1)
-
-    def sweep():
-        for K, N, h in handles:
-            for M in DECODE_M:
-                a, c = acts[(M, K)], outs[(M, N)]
-                ref.lib.i4_matmul(ctypes.c_void_p(h), a.ctypes.data, M, c.ctypes.data)
-
-    sweep()
+    rc = _RefCalls(ref, wl.cpu_calls(), threads)
+    rc.step()
     t0 = time.perf_counter()
     for _ in range(samples):
-        sweep()
+        rc.step()
     dt = time.perf_counter() - t0
-    step_bytes = sum(alg_bytes(M, K, N, 8) for K, N, _ in handles for M in DECODE_M)
-    for _, _, h in handles:
-        ref.free(h)
-    return {"value": round(step_bytes * samples / dt / 1e9, 2), "unit": "GB/s", "cores": threads,
+    value = wl.value(rc.amount(wl) * samples, dt)
+    rc.free()
+    return {"value": round(value, 4 if wl.unit == "TOPS" else 2), "unit": wl.unit, "cores": threads,
             "kind": "reference", "ms_per_step": round(dt / samples * 1e3, 2),
-            "sample": f"{samples} full decode sweeps (12 i4_matmul calls each) after 1 warm-up, "
-                      f"set_hi_prec(1), OpenMP {threads} threads, OMP_PROC_BIND=spread"}
+            "sample": f"{samples} x {wl.cpu_sample} after 1 warm-up, set_hi_prec(1), "
+                      f"OpenMP {threads} threads, OMP_PROC_BIND=spread"}
 
 
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
         return
+    wl = WORKLOADS[args.workload]()
     os.environ.setdefault("OMP_PROC_BIND", "spread")
     os.environ.setdefault("OMP_PLACES", "cores")
     ref, why = _reference_lib()
@@ -451,50 +602,37 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
     threads = os.cpu_count() or 1
-    handles = []
-    for i, (K, N) in enumerate(DECODE_SHAPES):
-        qw, sc = host_weights(K, N, 8, 100 + i)
-        handles.append((K, N, ref.prepack(qw, sc, None, K, N, 8)))
-        del qw
-    rng = np.random.default_rng(7)
-    acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32) for K, _ in DECODE_SHAPES for M in DECODE_M}
-    outs = {(M, N): np.empty((M, N), np.float32) for _, N in DECODE_SHAPES for M in DECODE_M}
-    ref.lib.i4_set_threads(threads)
-    ref.lib.i4_set_hi_prec(1)
-
-    def sweep():
-        for K, N, h in handles:
-            for M in DECODE_M:
-                ref.lib.i4_matmul(ctypes.c_void_p(h), acts[(M, K)].ctypes.data, M, outs[(M, N)].ctypes.data)
-
+    spec = wl.cpu_calls() if wl.name == "decode" else [(wl.K, wl.N, wl.bits, wl.Ms)]
+    rc = _RefCalls(ref, spec, threads)
     for _ in range(args.warmup):
-        sweep()
+        rc.step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        sweep()
+        rc.step()
     dt = time.perf_counter() - t0
-    step_bytes = sum(alg_bytes(M, K, N, 8) for K, N, _ in handles for M in DECODE_M)
-    value = step_bytes * args.steps / dt / 1e9
-    for _, _, h in handles:
-        ref.free(h)
-    line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "impl": "reference",
+    value = wl.value(rc.amount(wl) * args.steps, dt)
+    rc.free()
+    cfg = wl.config(1)
+    cfg["parallelism"] = f"host OpenMP, {threads} threads (rank 0 only)"
+    cfg.pop("timing", None)
+    cfg.pop("l2", None)
+    line = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32 (VPDPBUSD), f32 rescale",
             "data": "synthetic (random MatMulNBits codes, fp16 scales; N(0,1) activations)",
-            "config": {"workload": "configs[1]: INT8 decode GEMV sweep", "M": DECODE_M,
-                       "shapes_KN": DECODE_SHAPES, "activations": "two-pass INT16 (set_hi_prec(1))",
-                       "parallelism": f"host OpenMP, {threads} threads (rank 0 only)"},
-            "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads, "kind": "reference",
-                             "sample": f"{args.steps} full sweeps after {args.warmup} warm-ups"},
-            "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": cfg,
+            "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "reference",
+                             "sample": f"{args.steps} full steps after {args.warmup} warm-ups"},
+            "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def run_ncu_case(K, N, bits, M, launches=4):
     """One layer (N(0, 0.02) weights, RTN-packed; INT8 per channel), activations
-    quantized once (two-pass), then `launches` decode-kernel launches rotating
-    over enough weight copies that each launch streams from HBM."""
+    quantized once (two-pass), then `launches` matmul-kernel launches (the decode
+    kernel up to 64 tokens, the tensor-core GEMM above) rotating over enough
+    weight copies that each launch streams its weights from HBM."""
     import torch
     from breeze_engine_b200 import _lib as L
     lib = L.load()
@@ -513,7 +651,8 @@ def run_ncu_case(K, N, bits, M, launches=4):
     torch.cuda.synchronize()
     layer.free()
     print(json.dumps({"ncu_case": [K, N, bits, M], "launches": launches, "copies": copies,
-                      "alg_bytes_per_launch": decode_kernel_bytes(M, K, N, bits)}))
+                      "alg_bytes_per_launch": decode_kernel_bytes(M, K, N, bits),
+                      "alg_ops_per_launch": prefill_ops(M, K, N)}))
 
 
 def main(argv=None):
@@ -522,10 +661,11 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", metavar="K,N,BITS,M", default=None,
-                    help="profiling driver: pack one layer, quantize once, run the decode kernel "
+                    help="profiling driver: pack one layer, quantize once, run the matmul kernel "
                          "4 times and exit (for ncu captures of a single launch)")
     args = ap.parse_args(argv)
     if args.warmup < 3:

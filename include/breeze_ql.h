@@ -117,12 +117,16 @@ int ql_prepack_onnx_dev(const uint8_t* d_qw, const void* d_scales, const uint8_t
 int ql_weight_info(const void* handle, int* N, int* K, int* bits, int* device,
                    unsigned long long* bytes);
 
-/* Scratch bytes ql_matmul_dev_ws needs for M rows (quantized activations). */
+/* Scratch bytes ql_matmul_dev_ws needs for M rows (quantized activations;
+ * M > 64 uses the tensor-core GEMM's record layout, so the size is not linear
+ * in M across that boundary). */
 size_t ql_workspace_bytes(const void* handle, int M);
 
 /* Device twin of i4_matmul (kernel/quantized_matmul.cpp:528): dA [M,K] fp32
  * (16-byte aligned), dC [M,N] fp32, asynchronous on `stream`, with the
- * caller's workspace of at least ql_workspace_bytes(handle, M) bytes. */
+ * caller's workspace (16-byte aligned) of at least ql_workspace_bytes(handle, M)
+ * bytes.  Up to 64 rows run the weight-streaming decode kernel; more rows run
+ * the tcgen05 GEMM.  Both give the reference's bits. */
 int ql_matmul_dev_ws(void* handle, const float* dA, int M, float* dC, void* ws, size_t ws_bytes,
                      void* stream);
 
