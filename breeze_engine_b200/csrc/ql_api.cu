@@ -186,20 +186,17 @@ int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS,
 }
 
 // Quantize + matmul into a caller workspace of >= ws_bytes_for(M, nblk) bytes.
-// With one chunk the matmul is launched with PDL so it streams weights while
-// the quantizer finishes.
+// Every kernel of the chain is launched with programmatic dependent launch and
+// triggers its dependents early, so the next kernel streams its weights while
+// the previous one drains; each waits (griddepcontrol.wait) for its predecessor
+// before it reads activations or writes anything.
 int run_matmul(const Weight* w, const float* dA, int M, float* dC, int32_t* dCS, void* ws,
                size_t ws_bytes, cudaStream_t stream, bool hi_prec) {
     if (ws_bytes < ws_bytes_for(M, w->nblk) || reinterpret_cast<uintptr_t>(ws) % 16)
         return set_status(QL_EINVAL);        // bulk copies read the workspace in 16-byte units
-    if (M <= MAX_DECODE_TOKENS) {
-        int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
-        if (rc != QL_OK) return rc;
-        return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/true);
-    }
     int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
     if (rc != QL_OK) return rc;
-    return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/false);
+    return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/true);
 }
 
 }  // namespace
@@ -519,7 +516,7 @@ QL_API int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_p
     if (cudaGetDevice(&dev) != cudaSuccess) return set_status(QL_ECUDA);
     const auto* w = static_cast<const Weight*>(handle);
     if (dev != w->device) return set_status(QL_EDEVICE);
-    return run_compute(w, ws, M, dC, nullptr, static_cast<cudaStream_t>(stream), hi_prec != 0, false);
+    return run_compute(w, ws, M, dC, nullptr, static_cast<cudaStream_t>(stream), hi_prec != 0, true);
 }
 
 // ------------------------------------------------------------------ no-allocation variant

@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();   // the next kernel waits for this grid before touching its data
     // Seed both accumulator slots: the MMAs accumulate onto the bit patterns of
     // 1.5*2^31 (hi columns) and 1.5*2^23 (lo columns), so the sums come out of
     // TMEM already in the form the exact int->float conversion needs; the

@@ -103,6 +103,10 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
         fence_mbar_init();
     }
     __syncthreads();
+    // The next kernel on the stream (the next layer's quantizer or matmul) may
+    // be scheduled now: it waits for this grid's completion before it touches
+    // anything this grid reads or writes, and meanwhile prefetches its weights.
+    pdl_launch_dependents();
 
     if (warp == consumers) {
         // ------------------------------------------------------------ producer

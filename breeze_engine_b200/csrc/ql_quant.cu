@@ -30,8 +30,11 @@ template <bool HP>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ A, int lda,
                                                            int M, int K, ActView out) {
     // Let a dependent (PDL) kernel start its weight streaming right away; it
-    // still waits for this grid's completion before reading the planes.
+    // still waits for this grid's completion before reading the planes.  This
+    // grid itself may have started before its predecessor finished (it is
+    // launched with PDL too): wait for it before reading A or writing planes.
     pdl_launch_dependents();
+    pdl_wait();
     const int nblk = K / BLOCK_K;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(out.TPBA) * nblk) return;
@@ -112,6 +115,7 @@ template <bool HP>
 __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restrict__ A, int lda, int M, int K,
                                                             int m_tiles, uint8_t* __restrict__ out) {
     pdl_launch_dependents();
+    pdl_wait();                 // launched with PDL: the predecessor may still run
     const int nblk = K / BLOCK_K;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(m_tiles) * 128 * nblk) return;
@@ -173,17 +177,33 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
     *reinterpret_cast<uint4*>(rec + 4096 + o + 2048) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
 }
 
+// Launches a quantizer with programmatic dependent launch: it may start while
+// the previous kernel on the stream (a matmul of the previous layer) drains,
+// and waits for it with griddepcontrol.wait before touching memory.
+template <typename... Args>
+static cudaError_t launch_pdl(void (*kern)(Args...), unsigned grid, unsigned threads, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
                                  cudaStream_t stream) {
     const int m_tiles = (M + 127) / 128;
     const long long total = static_cast<long long>(m_tiles) * 128 * (K / BLOCK_K);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-    if (hi_prec)
-        quantize_gemm_kernel<true><<<grid, threads, 0, stream>>>(A, lda, M, K, m_tiles, out);
-    else
-        quantize_gemm_kernel<false><<<grid, threads, 0, stream>>>(A, lda, M, K, m_tiles, out);
-    return cudaGetLastError();
+    if (hi_prec) return launch_pdl(quantize_gemm_kernel<true>, grid, threads, stream, A, lda, M, K, m_tiles, out);
+    return launch_pdl(quantize_gemm_kernel<false>, grid, threads, stream, A, lda, M, K, m_tiles, out);
 }
 
 // Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
@@ -249,11 +269,8 @@ cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_p
     const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-    if (hi_prec)
-        quantize_act_kernel<true><<<grid, threads, 0, stream>>>(A, lda, M, K, out);
-    else
-        quantize_act_kernel<false><<<grid, threads, 0, stream>>>(A, lda, M, K, out);
-    return cudaGetLastError();
+    if (hi_prec) return launch_pdl(quantize_act_kernel<true>, grid, threads, stream, A, lda, M, K, out);
+    return launch_pdl(quantize_act_kernel<false>, grid, threads, stream, A, lda, M, K, out);
 }
 
 cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,
