@@ -161,24 +161,35 @@ class ClockSampler:
 
 
 class Layer:
-    """One packed weight (possibly several rotation copies) of a (K, N) layer shard."""
+    """One packed weight (possibly several rotation copies) of a (K, N) layer shard.
 
-    def __init__(self, lib, K, N, bits, world, rank, seed, copies):
+    ``mode='col'``: rank r keeps output rows [r N/P, (r+1) N/P) (column-parallel);
+    ``mode='row'``: rank r keeps input blocks [r K/P, (r+1) K/P) (row-parallel)."""
+
+    def __init__(self, lib, K, N, bits, world, rank, seed, copies, mode="col"):
         import torch
         from breeze_engine_b200 import backend
         from breeze_engine_b200.quant import quantize_matmul_nbits_torch
-        self.K, self.N, self.bits = K, N, bits
-        self.n_local = N // world
+        self.K, self.N, self.bits, self.mode = K, N, bits, mode
+        self.n_local = N // world if mode == "col" else N
+        self.k_local = K if mode == "col" else K // world
+        self.k0 = 0 if mode == "col" else rank * self.k_local
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
         w = torch.randn((K, N), generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
         qw, sc, qz = quantize_matmul_nbits_torch(w, bits=bits, per_channel=(bits == 8))
         del w
-        n0 = rank * self.n_local
-        qw = qw[n0:n0 + self.n_local].contiguous()
-        sc = sc.reshape(N, K // 32)[n0:n0 + self.n_local].contiguous()
-        self.handles = [backend.prepack(qw, sc, None, K, self.n_local, bits) for _ in range(copies)]
-        self.shard_bytes = self.n_local * K * bits // 8 + 2 * self.n_local * (K // 32)
+        nblk = K // 32
+        if mode == "col":
+            n0 = rank * self.n_local
+            qw = qw[n0:n0 + self.n_local].contiguous()
+            sc = sc.reshape(N, nblk)[n0:n0 + self.n_local].contiguous()
+        else:
+            b0, nb = self.k0 // 32, self.k_local // 32
+            qw = qw.reshape(N, nblk, -1)[:, b0:b0 + nb].contiguous()
+            sc = sc.reshape(N, nblk)[:, b0:b0 + nb].contiguous()
+        self.handles = [backend.prepack(qw, sc, None, self.k_local, self.n_local, bits) for _ in range(copies)]
+        self.shard_bytes = self.n_local * self.k_local * bits // 8 + 2 * self.n_local * (self.k_local // 32)
         del qw, sc
         torch.cuda.empty_cache()
 
@@ -186,7 +197,6 @@ class Layer:
         from breeze_engine_b200 import backend
         for h in self.handles:
             backend.free(h)
-
 
 
 # ------------------------------------------------------------------ workloads
@@ -318,7 +328,113 @@ class PrefillWorkload:
     cpu_sample = "i4_matmul calls at M=128 (the smallest prefill size)"
 
 
-WORKLOADS = {"decode": DecodeWorkload, "prefill": PrefillWorkload}
+class _OpsOrBytes:
+    """Shared metric logic: HBM bytes for decode-sized M, INT8 ops for prefill-sized M."""
+    bits = 4
+
+    def __init__(self):
+        self.unit = "GB/s" if self.M <= 64 else "TOPS"
+        self.kernel = ("decode_kernel (ql_gemv.cu)" if self.M <= 64
+                       else "gemm_kernel (ql_gemm.cu, tcgen05 kind::i8)")
+
+    def step_amount(self, calls):
+        if self.unit == "GB/s":
+            return sum(alg_bytes(M, layer.K, layer.N, layer.bits) for layer, _, M in calls)
+        return sum(prefill_ops(M, layer.K, layer.N) for layer, _, M in calls)
+
+    def value(self, amount, seconds):
+        return amount / seconds / (1e9 if self.unit == "GB/s" else 1e12)
+
+    def kernel_amount(self, M, K, n_local, bits):
+        return decode_kernel_bytes(M, K, n_local, bits) if self.unit == "GB/s" else prefill_ops(M, K, n_local)
+
+    def roofline(self, achieved, kern_amount_avg, calls, clock_mhz):
+        if self.unit == "GB/s":
+            return DecodeWorkload.roofline(self, achieved, kern_amount_avg, calls, clock_mhz)
+        return PrefillWorkload.roofline(self, achieved, kern_amount_avg, calls, clock_mhz)
+
+
+class LayerSetWorkload(_OpsOrBytes):
+    """the 27B-class decoder-layer projection set, 7 sequential calls."""
+    shapes = [("q", 5120, 6144), ("k", 5120, 1024), ("v", 5120, 1024), ("o", 6144, 5120),
+              ("gate", 5120, 17408), ("up", 5120, 17408), ("down", 17408, 5120)]
+
+    def __init__(self, M):
+        self.M = M
+        self.name = f"layer_m{M}"
+        super().__init__()
+        self.metric = (f"27B-class layer projection set, M={M}: "
+                       + ("HBM throughput" if self.unit == "GB/s" else "INT8 TOPS (4*M*N*K per call)"))
+
+    def build(self, lib, world, rank):
+        total = sum(K * N // 2 for _, K, N in self.shapes) // world
+        copies = int(min(4, max(1, -(-2 * L2_BYTES // total))))
+        layers = [Layer(lib, K, N, self.bits, world, rank, 4000 + i, copies)
+                  for i, (_, K, N) in enumerate(self.shapes)]
+        acts = {(self.M, K): _outlier_acts(self.M, K, 21 + K) for K in sorted({K for _, K, _ in self.shapes})}
+        calls = [(layer, layer.handles[0], self.M) for layer in layers]
+        self._rot = copies
+        return layers, acts, calls
+
+    def config(self, world):
+        return {"workload": f"configs[3]: 27B-class layer projection set, M={self.M}",
+                "layers_KN": {n: [K, N] for n, K, N in self.shapes},
+                "weights": "INT4 symmetric RTN, fp16 scales (block 32)",
+                "activations": "two-pass INT16 (hi_prec=1); N(0,1), 1% channels x20",
+                "l2": "7-call step touches > L2 (192 MB of weights)",
+                "timing": "CUDA graph of one step (7 quantize+matmul calls), CUDA events",
+                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+
+    def cpu_calls(self):
+        return [(K, N, self.bits, [min(self.M, 128)]) for _, K, N in self.shapes]
+
+    @property
+    def cpu_sample(self):
+        return f"7-call layer sets at M={min(self.M, 128)}"
+
+
+class ShardedWorkload(_OpsOrBytes):
+    """column-parallel K=8192, N=65536 (all-gather of C) and
+    row-parallel K=65536, N=8192 (reduce-scatter of FP32 partials), INT4."""
+
+    def __init__(self, M):
+        self.M = M
+        self.name = f"sharded_m{M}"
+        super().__init__()
+        self.metric = (f"sharded INT4 linear (column- and row-parallel), M={M}: "
+                       + ("HBM throughput" if self.unit == "GB/s" else "INT8 TOPS (4*M*N*K per call)"))
+
+    def build(self, lib, world, rank):
+        shard = (8192 * 65536 // 2) // world
+        copies = int(min(4, max(1, -(-2 * L2_BYTES // (2 * shard)))))
+        col = Layer(lib, 8192, 65536, self.bits, world, rank, 5000, copies, mode="col")
+        row = Layer(lib, 65536, 8192, self.bits, world, rank, 5001, copies, mode="row")
+        acts = {(self.M, 8192): _outlier_acts(self.M, 8192, 31), (self.M, 65536): _outlier_acts(self.M, 65536, 32)}
+        calls = [(col, col.handles[0], self.M), (row, row.handles[0], self.M)]
+        return [col, row], acts, calls
+
+    def config(self, world):
+        return {"workload": f"configs[4]: sharded INT4 linear, M={self.M}",
+                "column_parallel_KN": [8192, 65536], "row_parallel_KN": [65536, 8192],
+                "weights": "INT4 symmetric RTN, fp16 scales (block 32); one seed, sliced per rank",
+                "activations": "two-pass INT16 (hi_prec=1); N(0,1), 1% channels x20",
+                "l2": "rotated weight copies; step working set > L2",
+                "timing": "CUDA graph of one step (2 sharded calls incl. NCCL), CUDA events",
+                "parallelism": (f"P={world}: column-parallel + NCCL all-gather, row-parallel + NCCL reduce-scatter"
+                                if world > 1 else "P=1 (no collective)")}
+
+    def cpu_calls(self):
+        m = min(self.M, 128)
+        return [(8192, 65536, self.bits, [m]), (65536, 8192, self.bits, [m])]
+
+    @property
+    def cpu_sample(self):
+        return f"the two layers at M={min(self.M, 128)}"
+
+
+WORKLOADS = {"decode": DecodeWorkload, "prefill": PrefillWorkload,
+             "layer_m1": lambda: LayerSetWorkload(1), "layer_m512": lambda: LayerSetWorkload(512),
+             "sharded_m1": lambda: ShardedWorkload(1), "sharded_m2048": lambda: ShardedWorkload(2048)}
 
 
 # ------------------------------------------------------------------ our arm
@@ -328,7 +444,7 @@ def run_ours(args):
     import torch.distributed as dist
     from breeze_engine_b200 import _lib as L
     from breeze_engine_b200 import backend
-    from breeze_engine_b200.sharded import gather_columns
+    from breeze_engine_b200.sharded import gather_columns, reduce_partials
 
     wl = WORKLOADS[args.workload]()
     rank, local_rank, world = dist_env()
@@ -341,23 +457,31 @@ def run_ours(args):
     backend.set_hi_prec(True)
 
     layers, acts, calls = wl.build(lib, world, rank)
-    outs, wss = {}, {}
+    outs, wss, local_a = {}, {}, {}
     for layer, h, M in calls:
         outs[(id(layer), M)] = torch.empty((M, layer.n_local), dtype=torch.float32, device="cuda")
         need = lib.ql_workspace_bytes(ctypes.c_void_p(h), M)
-        if (layer.K, M) not in wss or wss[(layer.K, M)].numel() < need:
-            wss[(layer.K, M)] = torch.empty(need, dtype=torch.uint8, device="cuda")
+        if (layer.k_local, M) not in wss or wss[(layer.k_local, M)].numel() < need:
+            wss[(layer.k_local, M)] = torch.empty(need, dtype=torch.uint8, device="cuda")
+        # row-parallel: this rank's contiguous K slice of the activations
+        local_a[(id(layer), M)] = (acts[(M, layer.K)] if layer.mode == "col" else
+                                   torch.empty((M, layer.k_local), dtype=torch.float32, device="cuda"))
 
     def step():
         s_ptr = torch.cuda.current_stream().cuda_stream
         for layer, h, M in calls:
-            a, c, ws = acts[(M, layer.K)], outs[(id(layer), M)], wss[(layer.K, M)]
+            a, c, ws = local_a[(id(layer), M)], outs[(id(layer), M)], wss[(layer.k_local, M)]
+            if layer.mode == "row":
+                a.copy_(acts[(M, layer.K)][:, layer.k0:layer.k0 + layer.k_local])
             rc = lib.ql_matmul_dev_ws(ctypes.c_void_p(h), a.data_ptr(), M, c.data_ptr(),
                                       ws.data_ptr(), ws.numel(), s_ptr)
             if rc:
                 raise RuntimeError(f"ql_matmul_dev_ws failed: {rc}")
             if world > 1:
-                gather_columns(c)
+                if layer.mode == "col":
+                    gather_columns(c)
+                else:
+                    reduce_partials(c, "scatter")
 
     def barrier():
         if world > 1:
@@ -419,18 +543,21 @@ def run_ours(args):
     # copies, captured in a graph and timed with CUDA events.
     qws = {}
     for layer, h, M in calls:
-        key = (M, layer.K)
+        key = (id(layer), M)
         if key not in qws:
-            n = lib.ql_act_workspace_bytes(M, layer.K)
+            a = local_a[key]
+            if layer.mode == "row":
+                a.copy_(acts[(M, layer.K)][:, layer.k0:layer.k0 + layer.k_local])
+            n = lib.ql_act_workspace_bytes(M, layer.k_local)
             qws[key] = torch.empty(n, dtype=torch.uint8, device="cuda")
-            rc = lib.ql_quantize_act_dev(acts[key].data_ptr(), M, layer.K, 1, qws[key].data_ptr(), n,
+            rc = lib.ql_quantize_act_dev(a.data_ptr(), M, layer.k_local, 1, qws[key].data_ptr(), n,
                                          stream.cuda_stream)
             assert rc == 0
     torch.cuda.synchronize()
     REPS = 8 if wl.name == "decode" else 4
     kern_t, kern_amount, per_call = 0.0, 0, []
     for layer, h0, M in calls:
-        c, ws = outs[(id(layer), M)], qws[(M, layer.K)]
+        c, ws = outs[(id(layer), M)], qws[(id(layer), M)]
         gk = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gk):
             s_ptr = torch.cuda.current_stream().cuda_stream
@@ -441,10 +568,10 @@ def run_ours(args):
         gk.replay()
         nrep = max(2, args.steps // 2)
         dt = timed_replays(gk, nrep) / (nrep * REPS)
-        amt = wl.kernel_amount(M, layer.K, layer.n_local, layer.bits)
+        amt = wl.kernel_amount(M, layer.k_local, layer.n_local, layer.bits)
         kern_t += dt
         kern_amount += amt
-        per_call.append({"M": M, "K": layer.K, "N": layer.N, "us": round(dt * 1e6, 2),
+        per_call.append({"M": M, "K": layer.k_local, "N": layer.n_local, "us": round(dt * 1e6, 2),
                          wl.unit: round(wl.value(amt, dt), 1)})
         del gk
     achieved = wl.value(kern_amount, kern_t)
@@ -455,12 +582,12 @@ def run_ours(args):
     # ---- end to end through the reference-compatible host C ABI (i4_matmul)
     e2e = None
     if not args.no_e2e:
-        host_a = {k: v.cpu().pin_memory() for k, v in acts.items()}
+        host_a = {k: v.cpu().pin_memory() for k, v in local_a.items()}
         host_c = {k: torch.empty(tuple(v.shape), dtype=torch.float32).pin_memory() for k, v in outs.items()}
 
         def e2e_step():
             for layer, h, M in calls:
-                a = host_a[(M, layer.K)]
+                a = host_a[(id(layer), M)]
                 c = host_c[(id(layer), M)]
                 lib.i4_matmul(ctypes.c_void_p(h), ctypes.c_void_p(a.data_ptr()), M, ctypes.c_void_p(c.data_ptr()))
             return lib.ql_last_status()
@@ -473,10 +600,10 @@ def run_ours(args):
             e2e_step()
         t_e2e = max_over_ranks(time.perf_counter() - t0)
         e2e = {"value": round(wl.value(step_amount * args.steps, t_e2e), 2), "unit": wl.unit,
-               "h2d_bytes_per_step": int(sum(4 * M * layer.K for layer, _, M in calls)),
+               "h2d_bytes_per_step": int(sum(4 * M * layer.k_local for layer, _, M in calls)),
                "d2h_bytes_per_step": int(sum(4 * M * layer.n_local for layer, _, M in calls)),
                "api": "i4_matmul (host pointers, pinned buffers, synchronous)"
-                      + ("; output stays column-sharded per rank" if world > 1 else "")}
+                      + ("; outputs stay sharded per rank (no collective)" if world > 1 else "")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -559,7 +686,7 @@ class _RefCalls:
                                        self.outs[(M, N)].ctypes.data)
 
     def amount(self, wl):
-        if wl.name == "decode":
+        if wl.unit == "GB/s":
             return sum(alg_bytes(M, K, N, bits) for K, N, bits, Ms, _ in self.handles for M in Ms)
         return sum(prefill_ops(M, K, N) for K, N, _, Ms, _ in self.handles for M in Ms)
 
@@ -602,7 +729,8 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
     threads = os.cpu_count() or 1
-    spec = wl.cpu_calls() if wl.name == "decode" else [(wl.K, wl.N, wl.bits, wl.Ms)]
+    spec = ([(wl.K, wl.N, wl.bits, wl.Ms)] if wl.name == "prefill" else
+            [(K, N, b, [wl.M]) for K, N, b, _ in wl.cpu_calls()] if hasattr(wl, "M") else wl.cpu_calls())
     rc = _RefCalls(ref, spec, threads)
     for _ in range(args.warmup):
         rc.step()
