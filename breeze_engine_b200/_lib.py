@@ -29,6 +29,7 @@ SIGNATURES = [
     ("ql_version", _i, []),
     ("ql_device_count", _i, []),
     ("ql_get_hi_prec", _i, []),
+    ("ql_set_prefill_kernel", _i, [_i]),
     ("ql_last_status", _i, []),
     ("ql_error_string", ctypes.c_char_p, [_i]),
     ("ql_last_cuda_error_string", ctypes.c_char_p, []),

@@ -36,6 +36,7 @@
 #include <cstdlib>
 #include "ql_common.cuh"
 #include "ql_internal.h"
+#include "ql_tcgen05.cuh"
 
 namespace ql {
 
@@ -53,79 +54,6 @@ constexpr int A_SLOT = TILE_N * 32;    // canonical s8 weight tile per block (4 
 constexpr int NA = 4;                  // canonical weight slots
 constexpr uint32_t TMEM_COLS = 512;    // two accumulator slots of hi|lo x 128 columns
 
-__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
-    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
-    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
-    d |= static_cast<uint64_t>(1) << 46;      // tcgen05 descriptor version; SWIZZLE_NONE, base offset 0
-    return d;
-}
-
-// kind::i8 instruction descriptor: D = S32, A/B signedness, N >> 3, M >> 4.
-__host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N, bool a_signed, bool b_signed) {
-    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) |
-           (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-                 :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Writes the 32-bit value v to 8 consecutive columns of the warp's 32 lanes.
-__device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "r"(taddr), "r"(v) : "memory");
-}
-// Shared-memory float4 load kept in program order (volatile), so the
-// compiler cannot hoist a whole block's activation scales into registers.
-__device__ __forceinline__ float4 lds_f4(const float* ptr) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(smem_u32(ptr)));
-    return v;
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// Bounded wait that also gives up when another role raised the CTA's abort flag.
-__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    while (true) {
-        // suspended until the phase completes (or 10 us pass), so idle roles
-        // take no issue slots from the epilogue
-        if (mbar_try_wait_sleep(bar, parity, 10000)) return true;
-        if (*abort_flag) return false;
-        if (global_ns() - t0 > WAIT_LIMIT_NS) break;
-    }
-    record_error(err, QL_ETIMEOUT);
-    *abort_flag = 1;
-    return false;
-}
-
-// Warp-collective form: every lane waits (each observes the phase, so each sees
-// the bulk-copy / tensor-core writes it guards) and the outcome is made
-// uniform, so no lane continues into a .sync.aligned instruction alone.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag) {
-    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, err, abort_flag));
-}
 
 }  // namespace
 
@@ -546,6 +474,8 @@ size_t gemm_act_bytes(int M, int nblk) {
 
 cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec, float* C, int ldc,
                         int32_t* cs, cudaStream_t stream) {
+    if (prefill_kernel() != QL_PREFILL_I8 && gemm16_supports(w, hi_prec))
+        return launch_gemm16(w, act, M, C, ldc, cs, stream);
     GemmParams p = {};
     p.W = w->W;
     p.act = act;

@@ -83,6 +83,15 @@ cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_
 cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec, float* C, int ldc,
                         int32_t* cs, cudaStream_t stream);
 
+// INT4 weights with fp16 scales in two-pass mode also have a kind::f16 GEMM
+// (ql_gemm16.cu) on the same activation records; launch_gemm picks it unless
+// the prefill kernel selector (ql_set_prefill_kernel) asks for kind::i8.
+bool gemm16_supports(const Weight* w, bool hi_prec);
+cudaError_t launch_gemm16(const Weight* w, const uint8_t* act, int M, float* C, int ldc, int32_t* cs,
+                          cudaStream_t stream);
+enum : int { QL_PREFILL_AUTO = 0, QL_PREFILL_I8 = 1 };
+int prefill_kernel();                                    // ql_api.cu
+
 // Size of the fixed scratch behind ql_matmul_dev_noalloc (ql_api.cu); the
 // public header states the same value as QL_NOALLOC_SCRATCH_BYTES.
 constexpr size_t QL_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;

@@ -99,6 +99,14 @@ int ql_device_count(void);
 /* Current activation mode (the value last given to i4_set_hi_prec). */
 int ql_get_hi_prec(void);
 
+/* Prefill kernel selector (no counterpart in the reference, whose i4_matmul
+ * has one CPU path): 0 = automatic -- M > 64 tokens with INT4 weights, fp16
+ * scales and two-pass activations run the tcgen05 kind::f16 GEMM, every other
+ * prefill the kind::i8 GEMM; 1 = always the kind::i8 GEMM.  Both kernels give
+ * the reference's bits; the switch exists for comparison and testing.
+ * Process-global; returns QL_EINVAL for any other value. */
+int ql_set_prefill_kernel(int kind);
+
 /* Status of this thread's last call, and its description. */
 int ql_last_status(void);
 const char* ql_error_string(int code);

@@ -5,7 +5,9 @@ own activation records (ql_quant.cu).  The shapes here hit its tails: token
 tiles of 128 with a ragged last tile, weight tiles of 8 row groups with a
 ragged last tile, and block counts that leave a partial stage of 4 blocks.
 The bar is the same as for the decode kernel: FP32 outputs and INT32 block
-sums bit-identical to the reference algorithm.
+sums bit-identical to the reference algorithm.  INT4 weights with fp16 scales
+in two-pass mode have two GEMMs (tcgen05 kind::f16 and kind::i8); every test
+runs under both.
 """
 import ctypes
 
@@ -19,9 +21,15 @@ from conftest import bits_equal
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True)
-def _mode_reset():
-    yield
+@pytest.fixture(autouse=True, params=["auto", "i8"])
+def prefill_kernel(request):
+    """Every test runs twice: with the automatic choice (the kind::f16 GEMM for
+    INT4 weights with fp16 scales in two-pass mode, else kind::i8) and with the
+    kind::i8 GEMM forced (ql_set_prefill_kernel(1))."""
+    lib = qlc.lib()
+    assert lib.ql_set_prefill_kernel(0 if request.param == "auto" else 1) == 0
+    yield request.param
+    lib.ql_set_prefill_kernel(0)
     qlc.set_hi_prec(False)
     assert qlc.device_error() == 0
 
