@@ -62,16 +62,18 @@ namespace {
 constexpr int T_N = 128;                 // weight rows per tile (MMA M)
 constexpr int T_M = 128;                 // tokens per tile (MMA N)
 constexpr int T_G = T_N / 16;            // 16-row weight groups per tile
-constexpr int N_UNP = 2;                 // weight unpack warps
+constexpr int N_UNP = 2;                 // weight unpack warps (4 row groups each)
 constexpr int N_EPI = 8;                 // epilogue warps
 constexpr int N_CONV = 4;                // activation convert warps
-constexpr int N_WARPS = 4 + N_EPI + N_CONV;
+constexpr int N_WARPS = 2 + N_UNP + N_EPI + N_CONV;
 constexpr int E_COLS = 64;               // token columns per epilogue thread
 constexpr int A_BYTES = T_N * 32 * 2;    // FP16 weight tile per block: 128 rows x 32 k (8 KB)
 constexpr int B_BYTES = T_M * 64 * 2;    // FP16 activation tiles per block: h and l/256, 128 x 32 k each (16 KB)
 constexpr int N_ASLOT = 4;               // weight tile ring
 constexpr int N_BSLOT = 3;               // activation tile ring
 constexpr int N_ACC = 4;                 // TMEM accumulator slots of 128 columns
+constexpr int N_SC = 8;                  // scale ring: 256*bscale of 128 rows + ascale of 128 tokens per block
+constexpr int SC_BYTES = 1024;
 constexpr uint32_t TMEM_NCOLS = 512;
 constexpr int AREC16 = GEMM_AREC;        // INT8 activation record (ql_quant.cu)
 
@@ -83,15 +85,23 @@ __device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
 
 // 8 INT4 weights of one record word (byte i = q(row g, k_i) | q(row g+8, k_i) << 4)
 // -> exact FP16 (q - zp): rows g and g+8, k_0..k_3 each as two half2 words.
-// zg / zg8 are the half2 bit patterns of 1024 + zp for the two rows; the magic
-// 0x6400 | q is the FP16 value 1024 + q.
+// The bytes are first spread to (b0, b1) and (b2, b3) in the two halves of a
+// word; 0x6400 | q is the FP16 value 1024 + q (low nibble), 0x6400 | 16q is
+// 1024 + 16q (high nibble, scaled back by 1/16 in the same FMA).  zg / zg8 are
+// the half2 bit patterns of 1024 + zp and 64 + zp for rows g and g+8.
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 __device__ __forceinline__ void nib8_to_f16(uint32_t x, uint32_t zg, uint32_t zg8, uint2& rg, uint2& rg8) {
-    const uint32_t e02 = hsub2_bits((x & 0x000F000Fu) | 0x64006400u, zg);            // row g: k0, k2
-    const uint32_t e13 = hsub2_bits(((x >> 8) & 0x000F000Fu) | 0x64006400u, zg);     // row g: k1, k3
-    const uint32_t f02 = hsub2_bits(((x >> 4) & 0x000F000Fu) | 0x64006400u, zg8);    // row g+8: k0, k2
-    const uint32_t f13 = hsub2_bits(((x >> 12) & 0x000F000Fu) | 0x64006400u, zg8);   // row g+8: k1, k3
-    rg = make_uint2(__byte_perm(e02, e13, 0x5410), __byte_perm(e02, e13, 0x7632));
-    rg8 = make_uint2(__byte_perm(f02, f13, 0x5410), __byte_perm(f02, f13, 0x7632));
+    const uint32_t y01 = __byte_perm(x, 0, 0x0100);            // bytes b0 and b1 in the two halves
+    const uint32_t y23 = __byte_perm(x, 0, 0x0302);
+    constexpr uint32_t SIXTEENTH = 0x2C002C00u;                // 1/16 in both halves
+    rg = make_uint2(hsub2_bits((y01 & 0x000F000Fu) | 0x64006400u, zg),
+                    hsub2_bits((y23 & 0x000F000Fu) | 0x64006400u, zg));
+    rg8 = make_uint2(hfma2_bits((y01 & 0x00F000F0u) | 0x64006400u, SIXTEENTH, zg8),
+                     hfma2_bits((y23 & 0x00F000F0u) | 0x64006400u, SIXTEENTH, zg8));
 }
 
 // 4 bytes of the hi plane (stored as hi ^ 0x80) -> FP16 h = hi - 128:
@@ -123,7 +133,7 @@ struct Gemm16Params {
     int m_tiles, n_tiles, tiles;
     int BPS, STAGES;
     uint32_t stage_bytes, off_act;   // inside a stage: weights of 8 groups, then activations
-    uint32_t off_a, off_b, off_stages;
+    uint32_t off_a, off_b, off_sc, off_stages;
 };
 
 template <bool ZP, bool OUT_CS>
@@ -140,11 +150,14 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
     uint64_t* b_empty = b_full + N_BSLOT;
     uint64_t* acc_full = b_empty + N_BSLOT;
     uint64_t* acc_empty = acc_full + N_ACC;
-    uint64_t* drain = acc_empty + N_ACC;
+    uint64_t* sc_full = acc_empty + N_ACC;
+    uint64_t* sc_empty = sc_full + N_SC;
+    uint64_t* drain = sc_empty + N_SC;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
     uint8_t* a_ring = smem + p.off_a;
     uint8_t* b_ring = smem + p.off_b;
+    uint8_t* sc_ring = smem + p.off_sc;     // per block: 128 x f32 256*bscale, then 128 x f32 ascale
     uint8_t* stages = smem + p.off_stages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.STAGES; ++s) {
             mbar_init(smem_u32(&stage_full[s]), 1);
-            mbar_init(smem_u32(&stage_empty[s]), N_UNP + N_CONV + N_EPI);
+            mbar_init(smem_u32(&stage_empty[s]), N_UNP + N_CONV);
         }
         for (int a = 0; a < N_ASLOT; ++a) {
             mbar_init(smem_u32(&a_full[a]), N_UNP);
@@ -166,6 +179,10 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
         for (int k = 0; k < N_ACC; ++k) {
             mbar_init(smem_u32(&acc_full[k]), 1);
             mbar_init(smem_u32(&acc_empty[k]), N_EPI);
+        }
+        for (int k = 0; k < N_SC; ++k) {
+            mbar_init(smem_u32(&sc_full[k]), N_CONV);
+            mbar_init(smem_u32(&sc_empty[k]), N_EPI);
         }
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
@@ -256,9 +273,10 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
         if (lane == 0) mma_commit(smem_u32(drain));
         __syncwarp();
         mbar_wait(smem_u32(drain), 0, p.err);
-    } else if (warp < 4) {
+    } else if (warp < 4 || warp >= 4 + N_EPI + N_CONV) {
         // ------------------------------------------------------------ weight unpack
-        const int u = warp - 2;                           // row groups u, u+2, u+4, u+6
+        // warps 2, 3 and the last N_UNP - 2; warp u takes row groups u, u + N_UNP, ...
+        const int u = warp < 4 ? warp - 2 : warp - (4 + N_EPI + N_CONV) + 2;
         const int g = lane >> 2, t = lane & 3;
         // canonical FP16 offset of (row g of group gg, k 4t..4t+3): core-matrix
         // K column t/2 (2048 B apart), 8-row group 2gg (128 B apart), row g (16 B),
@@ -287,11 +305,12 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                         if (gg < groups) {
                             const uint8_t* rec = wst + gg * p.BPS * REC + j * REC;
                             const uint2 v = *reinterpret_cast<const uint2*>(rec + lane * 8);
-                            uint32_t zg = 0x64086408u, zg8 = 0x64086408u;      // 1024 + 8
+                            // 1024 + zp (row g) and -(64 + zp) (row g+8); zp = 8 by default
+                            uint32_t zg = 0x64086408u, zg8 = 0xD480D480u;
                             if (ZP) {
                                 const uint32_t z = rec[TB + SB + g];
                                 zg = (0x6400u | (z & 15u)) * 0x00010001u;
-                                zg8 = (0x6400u | (z >> 4)) * 0x00010001u;
+                                zg8 = (0xD400u | ((z >> 4) << 4)) * 0x00010001u;
                             }
                             nib8_to_f16(v.x, zg, zg8, r0, r1);
                             nib8_to_f16(v.y, zg, zg8, r2, r3);
@@ -310,7 +329,7 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                 if (ok && lane == 0) mbar_arrive(smem_u32(&stage_empty[s]));
             }
         }
-    } else if (warp >= 4 + N_EPI) {
+    } else if (warp >= 4 + N_EPI) {   // and < 4 + N_EPI + N_CONV
         // ------------------------------------------------------------ activation convert
         // Input record (per block): hi plane then lo plane, each [2 K halves][16
         // token groups][8 tokens x 16 B] (16 k per row).  Output: h chunks then
@@ -318,21 +337,35 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
         // tokens x 16 B] (8 k per row): one 16-byte input row of K half kh gives
         // the two 16-byte output rows of chunk kh.
         const int ct = (warp - 4 - N_EPI) * 32 + lane;   // 0..127
+        // the weight row whose scale this thread copies: group ct/16, entry
+        // 2*(r%8) + r/8 of the record's scales (entry 2g = row g, 2g+1 = row g+8)
+        const int cg = ct >> 4, cr = ct & 15, csidx = 2 * (cr & 7) + (cr >> 3);
         int si = 0, bi = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            const int nt = tile / p.m_tiles;
+            const bool row_ok = cg < min(T_G, p.G - nt * T_G);
             for (int ks = 0; ks < spt && ok; ++ks, ++si) {
                 const int s = si % p.STAGES;
                 if (!(ok = warp_wait(smem_u32(&stage_full[s]), (si / p.STAGES) & 1, p.err, abort_flag))) break;
                 const uint8_t* ast = stages + static_cast<size_t>(s) * p.stage_bytes + p.off_act;
                 const int nb = min(p.BPS, p.nblk - ks * p.BPS);
                 for (int j = 0; j < nb; ++j, ++bi) {
-                    const int bs = bi % N_BSLOT;
+                    const int bs = bi % N_BSLOT, sc = bi % N_SC;
                     if (bi >= N_BSLOT &&
                         !(ok = warp_wait(smem_u32(&b_empty[bs]), ((bi / N_BSLOT) - 1) & 1, p.err, abort_flag)))
                         break;
+                    if (bi >= N_SC &&
+                        !(ok = warp_wait(smem_u32(&sc_empty[sc]), ((bi / N_SC) - 1) & 1, p.err, abort_flag)))
+                        break;
                     const uint8_t* src = ast + j * AREC16;
                     uint8_t* dst = b_ring + bs * B_BYTES;
+                    // activation scale of token ct and 256*bscale of weight row ct
+                    // (exact: an exponent shift of the FP16 scale); 0 past the last row group
+                    float* scs = reinterpret_cast<float*>(sc_ring + sc * SC_BYTES);
+                    scs[128 + ct] = reinterpret_cast<const float*>(src + 8192)[ct];
+                    const uint8_t* wrec = stages + static_cast<size_t>(s) * p.stage_bytes + cg * p.BPS * REC + j * REC;
+                    scs[ct] = row_ok ? __half2float(reinterpret_cast<const __half*>(wrec + TB)[csidx]) * 256.0f : 0.0f;
 #pragma unroll
                     for (int rep = 0; rep < 2; ++rep) {
                         const int idx = ct + rep * 128;            // input row: kh*128 + tg*8 + r
@@ -351,7 +384,10 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(&b_full[bs]));
+                    if (lane == 0) {
+                        mbar_arrive(smem_u32(&b_full[bs]));
+                        mbar_arrive(smem_u32(&sc_full[sc]));
+                    }
                 }
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(smem_u32(&stage_empty[s]));
@@ -363,9 +399,8 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
         const int q = warp & 3;                           // TMEM lane quarter (hardware rule: warp % 4)
         const int cq = e >> 2;                            // token columns E_COLS*cq ..
         const int row = q * 32 + lane;                    // weight row within the tile
-        const int g16 = row >> 4, r16 = row & 15;
-        const int sidx = 2 * (r16 & 7) + (r16 >> 3);      // this row's entry in a record's scales
-        int si = 0, bi = 0;
+        const int g16 = row >> 4;
+        int bi = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
             const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
@@ -374,20 +409,15 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
             uint64_t acc[E_COLS / 2];                     // E_COLS token columns as f32x2 pairs
 #pragma unroll
             for (int i = 0; i < E_COLS / 2; ++i) acc[i] = 0;
-            for (int ks = 0; ks < spt && ok; ++ks, ++si) {
-                const int s = si % p.STAGES;
-                if (!(ok = warp_wait(smem_u32(&stage_full[s]), (si / p.STAGES) & 1, p.err, abort_flag))) break;
-                const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
+            for (int ks = 0; ks < spt && ok; ++ks) {
                 const int nb = min(p.BPS, p.nblk - ks * p.BPS);
                 for (int j = 0; j < nb; ++j, ++bi) {
-                    const int ac = bi % N_ACC;
+                    const int ac = bi % N_ACC, sc = bi % N_SC;
+                    if (!(ok = warp_wait(smem_u32(&sc_full[sc]), (bi / N_SC) & 1, p.err, abort_flag))) break;
                     if (!(ok = warp_wait(smem_u32(&acc_full[ac]), (bi / N_ACC) & 1, p.err, abort_flag))) break;
                     tc_fence_after();
-                    float bs = 0.0f;
-                    if (g16 < groups) {
-                        const uint8_t* rec = st + g16 * p.BPS * REC + j * REC;
-                        bs = __half2float(reinterpret_cast<const __half*>(rec + TB)[sidx]);
-                    }
+                    const float* scs = reinterpret_cast<const float*>(sc_ring + sc * SC_BYTES);
+                    const float bs256 = scs[row];                 // 256 * bscale (0 past the last row group)
                     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ac * T_M + cq * E_COLS;
                     if constexpr (OUT_CS) {
                         // block sums [M][N][nblk] = 256 * D (exact): a checking output
@@ -407,27 +437,29 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                         }
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[ac]));
+                        if (lane == 0) {
+                            mbar_arrive(smem_u32(&acc_empty[ac]));
+                            mbar_arrive(smem_u32(&sc_empty[sc]));
+                        }
+                        (void)bs256;
                     } else {
-                        // 256 * bscale is exact (an exponent shift of an FP16 value)
-                        const float bs256 = bs * 256.0f;
                         const uint64_t bs2 = f2_pack(bs256, bs256);
-                        const float* ascale = reinterpret_cast<const float*>(st + p.off_act + j * AREC16 + 8192) +
-                                              cq * E_COLS;
-                        // 16-column chunks; the next chunk's TMEM load is in flight while
+                        const float* ascale = scs + 128 + cq * E_COLS;
+                        // 8-column chunks; the next chunk's TMEM load is in flight while
                         // this one is rescaled; the slot is released as soon as its last
                         // chunk has been read
-                        uint32_t v[2][16];
-                        tmem_ld16(taddr, v[0]);
+                        constexpr int NCH = E_COLS / 8;
+                        uint32_t v[2][8];
+                        tmem_ld8(taddr, v[0]);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int cc = 0; cc < E_COLS / 16; ++cc) {
+                        for (int cc = 0; cc < NCH; ++cc) {
                             const int cur = cc & 1;
-                            if (cc < E_COLS / 16 - 1) tmem_ld16(taddr + (cc + 1) * 16, v[cur ^ 1]);
+                            if (cc < NCH - 1) tmem_ld8(taddr + (cc + 1) * 8, v[cur ^ 1]);
 #pragma unroll
-                            for (int k = 0; k < 16; k += 4) {
-                                const float4 a4 = lds_f4(ascale + cc * 16 + k);
-                                const int i0 = (cc * 16 + k) >> 1;
+                            for (int k = 0; k < 8; k += 4) {
+                                const float4 a4 = lds_f4(ascale + cc * 8 + k);
+                                const int i0 = (cc * 8 + k) >> 1;
                                 const uint64_t d0 = i2_pack(static_cast<int32_t>(v[cur][k]),
                                                             static_cast<int32_t>(v[cur][k + 1]));
                                 const uint64_t d1 = i2_pack(static_cast<int32_t>(v[cur][k + 2]),
@@ -435,9 +467,9 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                                 acc[i0] = f2_fma(f2_pack(a4.x, a4.y), f2_mul(d0, bs2), acc[i0]);
                                 acc[i0 + 1] = f2_fma(f2_pack(a4.z, a4.w), f2_mul(d1, bs2), acc[i0 + 1]);
                             }
-                            if (cc < E_COLS / 16 - 1) {
+                            if (cc < NCH - 1) {
                                 tmem_wait_ld();
-                                if (cc == E_COLS / 16 - 2) {
+                                if (cc == NCH - 2) {
                                     // every column of the slot is in registers: hand it back
                                     tc_fence_before();
                                     __syncwarp();
@@ -445,10 +477,10 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemm16_kernel(const Gemm16Par
                                 }
                             }
                         }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(&sc_empty[sc]));
                     }
                 }
-                __syncwarp();
-                if (ok && lane == 0) mbar_arrive(smem_u32(&stage_empty[s]));
             }
             if (!ok || OUT_CS) continue;
             // store C[m, n] for this thread's 64 token columns (lanes = consecutive n)
@@ -486,11 +518,12 @@ static cudaError_t gemm16_launch(const Gemm16Params& p0, cudaStream_t stream) {
     const uint32_t bar_bytes = 1024;                       // barriers, abort flag, TMEM address
     p.off_a = bar_bytes;
     p.off_b = p.off_a + N_ASLOT * A_BYTES;
-    p.off_stages = p.off_b + N_BSLOT * B_BYTES;
+    p.off_sc = p.off_b + N_BSLOT * B_BYTES;
+    p.off_stages = p.off_sc + N_SC * SC_BYTES;
     p.STAGES = 3;
-    while (p.STAGES > 2 && p.off_stages + static_cast<size_t>(p.STAGES) * p.stage_bytes > 220 * 1024) --p.STAGES;
+    while (p.STAGES > 2 && p.off_stages + static_cast<size_t>(p.STAGES) * p.stage_bytes > 227 * 1024) --p.STAGES;
     const size_t smem = p.off_stages + static_cast<size_t>(p.STAGES) * p.stage_bytes;
-    const size_t bars = (2 * p.STAGES + 2 * N_ASLOT + 2 * N_BSLOT + 2 * N_ACC + 1) * 8 + 16;
+    const size_t bars = (2 * p.STAGES + 2 * N_ASLOT + 2 * N_BSLOT + 2 * N_ACC + 2 * N_SC + 1) * 8 + 16;
     if (smem > 227 * 1024 || bars > bar_bytes || (p.off_act % 16) || (REC % 16) || (p.off_a % 1024) ||
         (p.off_b % 1024) || (p.off_stages % 1024))
         return cudaErrorInvalidConfiguration;
