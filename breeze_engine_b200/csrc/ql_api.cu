@@ -253,16 +253,18 @@ QL_API int ql_get_hi_prec(void) {
     return g_hi_prec;
 }
 
-// Prefill (M > 64) kernel selector: 0 = automatic (kind::f16 for INT4 weights
-// with fp16 scales in two-pass mode, else kind::i8), 1 = always kind::i8.
-// Both give the same bits; process-global like i4_set_hi_prec.
+// Prefill (M > 64) kernel selector: 0 = automatic (the single-CTA kind::f16
+// GEMM for INT4 weights with fp16 scales in two-pass mode, else kind::i8), 1 =
+// always kind::i8, 2 = the CTA-pair kind::f16 GEMM where it applies.  All give
+// the same bits; process-global like i4_set_hi_prec.
 static std::atomic<int> g_prefill_kernel{ql::QL_PREFILL_AUTO};
 namespace ql {
 int prefill_kernel() { return g_prefill_kernel.load(std::memory_order_relaxed); }
 }  // namespace ql
 
 QL_API int ql_set_prefill_kernel(int kind) {
-    if (kind != ql::QL_PREFILL_AUTO && kind != ql::QL_PREFILL_I8) return set_status(QL_EINVAL);
+    if (kind != ql::QL_PREFILL_AUTO && kind != ql::QL_PREFILL_I8 && kind != ql::QL_PREFILL_F16_PAIR)
+        return set_status(QL_EINVAL);
     g_prefill_kernel.store(kind, std::memory_order_relaxed);
     return set_status(QL_OK);
 }

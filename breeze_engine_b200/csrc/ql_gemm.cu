@@ -59,7 +59,7 @@ constexpr uint32_t TMEM_COLS = 512;    // two accumulator slots of hi|lo x 128 c
 
 struct GemmParams {
     const uint8_t* W;        // weight records [G][nblk][REC]
-    const uint8_t* act;      // GEMM activation records [m_tiles][nblk][AREC]
+    const uint8_t* act;      // GEMM activation buffer (token-half major, ql_internal.h)
     float* C;
     int32_t* CS;
     int* err;
@@ -70,11 +70,11 @@ struct GemmParams {
     uint32_t off_a, off_stages;      // inside dynamic shared memory
 };
 
-// GEMM activation record per (128-token tile, block) (GEMM_AREC bytes,
-// ql_internal.h): hi plane, lo plane (each [2 K halves][16 token groups][8
-// tokens x 16 B], the canonical K-major B operand), then 128 fp32 scales.
+// Activation stage layout (per stage of BPS blocks, after the weights):
+// [half 0 planes: BPS x GEMM_HPLANES][half 1 planes][scales: BPS x 128 fp32];
+// each half's hi / lo plane is the canonical K-major B operand of 64 tokens.
 constexpr int AREC = GEMM_AREC;
-static_assert(GEMM_AREC == 4096 + 4096 + TILE_M * 4, "GEMM activation record layout");
+static_assert(GEMM_AREC == 2 * GEMM_HPLANES + TILE_M * 4, "GEMM activation layout");
 
 template <int BITS, bool HALF, bool ZP, bool HP, bool OUT_CS>
 __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p) {
@@ -174,8 +174,11 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
                             bulk_g2s(base + g * p.BPS * REC, p.W + rec0 * REC, nb * REC, full);
                         }
                         if (!pdl_done) { pdl_wait(); pdl_done = true; }   // activations: previous grid
-                        bulk_g2s(base + p.off_act, p.act + (static_cast<size_t>(mt) * p.nblk + b0) * AREC,
-                                 nb * AREC, full);
+                        for (int h = 0; h < 2; ++h)
+                            bulk_g2s(base + p.off_act + h * p.BPS * GEMM_HPLANES,
+                                     p.act + gemm_planes_off(mt, h, b0, p.nblk), nb * GEMM_HPLANES, full);
+                        bulk_g2s(base + p.off_act + 2 * p.BPS * GEMM_HPLANES,
+                                 p.act + gemm_scales_off(mt, b0, p.m_tiles, p.nblk), nb * GEMM_SCALES, full);
                     }
                     __syncwarp();
                 }
@@ -187,8 +190,9 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
             // The whole warp waits (converged); lane 0 issues the MMAs and commits.
-            const uint32_t idesc_hi = make_idesc_i8(TILE_N, TILE_M, true, true);
-            const uint32_t idesc_lo = make_idesc_i8(TILE_N, TILE_M, true, !HP);
+            // one MMA per 64-token half and plane (N = 64)
+            const uint32_t idesc_hi = make_idesc_i8(TILE_N, TILE_M / 2, true, true);
+            const uint32_t idesc_lo = make_idesc_i8(TILE_N, TILE_M / 2, true, !HP);
             int si = 0, bi = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
@@ -206,10 +210,13 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
                         tc_fence_after();
                         if (lane == 0) {
                             const uint64_t da = make_smem_desc(smem_u32(a_ring + as * A_SLOT), 2048, 128);
-                            const uint32_t rec = act_base + j * AREC;
                             const uint32_t d_hi = tmem + ac * 256, d_lo = d_hi + 128;
-                            if (HP) mma_i8(d_hi, da, make_smem_desc(rec, 2048, 128), idesc_hi, 1);   // onto the seeds
-                            mma_i8(d_lo, da, make_smem_desc(rec + 4096, 2048, 128), idesc_lo, 1);
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t pl = act_base + (h * p.BPS + j) * GEMM_HPLANES;
+                                if (HP) mma_i8(d_hi + h * 64, da, make_smem_desc(pl, 1024, 128), idesc_hi, 1);   // onto the seeds
+                                mma_i8(d_lo + h * 64, da, make_smem_desc(pl + 2048, 1024, 128), idesc_lo, 1);
+                            }
                             mma_commit(smem_u32(&acc_full[ac]));
                             mma_commit(smem_u32(&a_empty[as]));
                         }
@@ -315,7 +322,8 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
                                   : reinterpret_cast<const float*>(rec + TB)[sidx];
                     }
                     const uint64_t bs2 = f2_pack(bs, bs);
-                    const float* ascale = reinterpret_cast<const float*>(st + p.off_act + j * AREC + 8192) + cq * ECOLS;
+                    const float* ascale = reinterpret_cast<const float*>(st + p.off_act + 2 * p.BPS * GEMM_HPLANES +
+                                                                         j * GEMM_SCALES) + cq * ECOLS;
                     const uint32_t t_hi = tmem + (static_cast<uint32_t>(q * 32) << 16) + ac * 256 + cq * ECOLS;
                     if constexpr (OUT_CS) {
                         // block sums [M][N][nblk]: a checking output, not a fast path

@@ -73,10 +73,26 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 
-// Prefill (M > MAX_DECODE_TOKENS) runs the tcgen05 GEMM (ql_gemm.cu) on
-// activations quantized into GEMM records: per (128-token tile, block) the hi
-// and lo planes as canonical K-major tcgen05 B operands, then 128 fp32 scales.
-constexpr int GEMM_AREC = 4096 + 4096 + 128 * 4;
+// Prefill (M > MAX_DECODE_TOKENS) runs the tcgen05 GEMMs (ql_gemm16.cu,
+// ql_gemm.cu) on activations quantized into a token-half-major buffer:
+//   planes  [m_tiles][2 halves][nblk][GEMM_HPLANES]: per 64-token half of a
+//           128-token tile and 32-wide block, the hi plane (hi - 128, s8; q8 in
+//           single-pass mode) then the lo plane (u8), each [2 K halves][8 token
+//           groups][8 tokens x 16 B] -- the canonical K-major tcgen05 B operand
+//           of 64 tokens (LBO 1024 B, SBO 128 B);
+//   scales  [m_tiles][nblk][128] fp32 activation scales, after all planes.
+// A half's planes are contiguous across blocks, so a stage of blocks of one
+// half is one bulk copy; tokens M..(tile end) are zeros.
+constexpr int GEMM_HPLANES = 4096;
+constexpr int GEMM_SCALES = 128 * 4;
+constexpr int GEMM_AREC = 2 * GEMM_HPLANES + GEMM_SCALES;   // bytes per (tile, block)
+__host__ __device__ inline size_t gemm_planes_off(int mt, int h, int b, int nblk) {
+    return ((static_cast<size_t>(mt) * 2 + h) * nblk + b) * GEMM_HPLANES;
+}
+__host__ __device__ inline size_t gemm_scales_off(int mt, int b, int m_tiles, int nblk) {
+    return static_cast<size_t>(m_tiles) * 2 * nblk * GEMM_HPLANES +
+           (static_cast<size_t>(mt) * nblk + b) * GEMM_SCALES;
+}
 size_t gemm_act_bytes(int M, int nblk);
 cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
                                  cudaStream_t stream);
@@ -89,7 +105,7 @@ cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec
 bool gemm16_supports(const Weight* w, bool hi_prec);
 cudaError_t launch_gemm16(const Weight* w, const uint8_t* act, int M, float* C, int ldc, int32_t* cs,
                           cudaStream_t stream);
-enum : int { QL_PREFILL_AUTO = 0, QL_PREFILL_I8 = 1 };
+enum : int { QL_PREFILL_AUTO = 0, QL_PREFILL_I8 = 1, QL_PREFILL_F16_PAIR = 2 };
 int prefill_kernel();                                    // ql_api.cu
 
 // Size of the fixed scratch behind ql_matmul_dev_noalloc (ql_api.cu); the

@@ -106,11 +106,11 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     }
 }
 
-// GEMM-layout variant (M > 64, ql_gemm.cu): one record of GEMM_AREC bytes per
-// (128-token tile, block): the hi plane (hi - 128, s8) and the lo plane (u8;
-// q8 in single-pass mode) as canonical K-major tcgen05 B operands
-// [2 K halves][16 groups of 8 tokens][8 tokens x 16 B], then 128 fp32 scales.
-// Tokens M..(tile end) are written as zeros.
+// GEMM-layout variant (M > 64, ql_gemm16.cu / ql_gemm.cu): the token-half-major
+// buffer of ql_internal.h -- per (64-token half, block) the hi plane (hi - 128,
+// s8; q8 in single-pass mode) and the lo plane (u8) as canonical K-major
+// tcgen05 B operands [2 K halves][8 groups of 8 tokens][8 tokens x 16 B], and
+// per (128-token tile, block) 128 fp32 scales.  Tokens M..(tile end) are zeros.
 template <bool HP>
 __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restrict__ A, int lda, int M, int K,
                                                             int m_tiles, uint8_t* __restrict__ out) {
@@ -121,17 +121,17 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
     if (idx >= static_cast<long long>(m_tiles) * 128 * nblk) return;
     const int m = static_cast<int>(idx / nblk);
     const int b = static_cast<int>(idx % nblk);
-    const int mt = m >> 7, mr = m & 127;
-    uint8_t* rec = out + (static_cast<size_t>(mt) * nblk + b) * GEMM_AREC;
-    const int o = (mr >> 3) * 128 + (mr & 7) * 16;            // K half 0; K half 1 at +2048
-    float* scales = reinterpret_cast<float*>(rec + 8192);
+    const int mt = m >> 7, mr = m & 127, tw = mr & 63;     // token within its 64-token half
+    uint8_t* planes = out + gemm_planes_off(mt, mr >> 6, b, nblk);
+    const int o = (tw >> 3) * 128 + (tw & 7) * 16;            // K half 0; K half 1 at +1024
+    float* scale = reinterpret_cast<float*>(out + gemm_scales_off(mt, b, m_tiles, nblk)) + mr;
     if (m >= M) {
         const uint4 z = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(rec + o) = z;
-        *reinterpret_cast<uint4*>(rec + o + 2048) = z;
-        *reinterpret_cast<uint4*>(rec + 4096 + o) = z;
-        *reinterpret_cast<uint4*>(rec + 4096 + o + 2048) = z;
-        scales[mr] = 0.0f;
+        *reinterpret_cast<uint4*>(planes + o) = z;
+        *reinterpret_cast<uint4*>(planes + o + 1024) = z;
+        *reinterpret_cast<uint4*>(planes + 2048 + o) = z;
+        *reinterpret_cast<uint4*>(planes + 2048 + o + 1024) = z;
+        *scale = 0.0f;
         return;
     }
     const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
@@ -149,9 +149,9 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
     }
     constexpr float QMAX = HP ? 32767.0f : 127.0f;
     constexpr int IMAX = HP ? 32767 : 127;
-    const float scale = __fdiv_rn(amax, QMAX);
-    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    scales[mr] = scale;
+    const float scl = __fdiv_rn(amax, QMAX);
+    const float inv = scl > 0.0f ? __fdiv_rn(1.0f, scl) : 0.0f;
+    *scale = scl;
     uint32_t hw[8], lw[8];
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
@@ -171,10 +171,10 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
         hw[w] = hword;
         lw[w] = lword;
     }
-    *reinterpret_cast<uint4*>(rec + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(rec + o + 2048) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-    *reinterpret_cast<uint4*>(rec + 4096 + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    *reinterpret_cast<uint4*>(rec + 4096 + o + 2048) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    *reinterpret_cast<uint4*>(planes + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(planes + o + 1024) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    *reinterpret_cast<uint4*>(planes + 2048 + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4*>(planes + 2048 + o + 1024) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
 }
 
 // Launches a quantizer with programmatic dependent launch: it may start while

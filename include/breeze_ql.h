@@ -102,8 +102,9 @@ int ql_get_hi_prec(void);
 /* Prefill kernel selector (no counterpart in the reference, whose i4_matmul
  * has one CPU path): 0 = automatic -- M > 64 tokens with INT4 weights, fp16
  * scales and two-pass activations run the tcgen05 kind::f16 GEMM, every other
- * prefill the kind::i8 GEMM; 1 = always the kind::i8 GEMM.  Both kernels give
- * the reference's bits; the switch exists for comparison and testing.
+ * prefill the kind::i8 GEMM; 1 = always the kind::i8 GEMM; 2 = the kind::f16
+ * GEMM on CTA pairs (cta_group::2) where it applies.  All kernels give the
+ * reference's bits; the switch exists for comparison and testing.
  * Process-global; returns QL_EINVAL for any other value. */
 int ql_set_prefill_kernel(int kind);
 

@@ -6,8 +6,8 @@ tiles of 128 with a ragged last tile, weight tiles of 8 row groups with a
 ragged last tile, and block counts that leave a partial stage of 4 blocks.
 The bar is the same as for the decode kernel: FP32 outputs and INT32 block
 sums bit-identical to the reference algorithm.  INT4 weights with fp16 scales
-in two-pass mode have two GEMMs (tcgen05 kind::f16 and kind::i8); every test
-runs under both.
+in two-pass mode have three GEMMs (tcgen05 kind::f16 on CTA pairs or single
+CTAs, and kind::i8); every test runs under each.
 """
 import ctypes
 
@@ -21,13 +21,17 @@ from conftest import bits_equal
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "i8"])
+_KINDS = {"auto": 0, "i8": 1, "f16_pair": 2}
+
+
+@pytest.fixture(autouse=True, params=list(_KINDS))
 def prefill_kernel(request):
-    """Every test runs twice: with the automatic choice (the kind::f16 GEMM for
-    INT4 weights with fp16 scales in two-pass mode, else kind::i8) and with the
-    kind::i8 GEMM forced (ql_set_prefill_kernel(1))."""
+    """Every test runs under each prefill kernel: the automatic choice (the
+    single-CTA kind::f16 GEMM for INT4 weights with fp16 scales in two-pass
+    mode, else kind::i8), the kind::i8 GEMM forced, and the kind::f16 GEMM on
+    CTA pairs (ql_set_prefill_kernel 0 / 1 / 2)."""
     lib = qlc.lib()
-    assert lib.ql_set_prefill_kernel(0 if request.param == "auto" else 1) == 0
+    assert lib.ql_set_prefill_kernel(_KINDS[request.param]) == 0
     yield request.param
     lib.ql_set_prefill_kernel(0)
     qlc.set_hi_prec(False)
