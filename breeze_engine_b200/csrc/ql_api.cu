@@ -7,6 +7,7 @@
 // pointers and are synchronous, so an unchanged ctypes or C++ caller works.
 // The ql_* entry points take device pointers and a cudaStream_t (as void*),
 // enqueue asynchronously and return an int status (0 = OK).
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -42,6 +43,8 @@ struct DeviceState {
     size_t buf_bytes = 0;
     void* ws = nullptr;              // workspace for ql_matmul_dev without a caller workspace
     size_t ws_bytes = 0;
+    cudaStream_t copy_stream = nullptr;   // i4_matmul: output copies overlapping the matmul
+    cudaEvent_t chunk_done[8] = {};       // i4_matmul: one per output column chunk
 };
 DeviceState g_dev[MAX_DEVICES];
 
@@ -173,13 +176,14 @@ int run_quantize(const float* dA, int M, int K, void* ws, cudaStream_t stream, b
 }
 
 int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS, cudaStream_t stream,
-                bool hi_prec, bool pdl) {
+                bool hi_prec, bool pdl, int ldc = 0) {
+    if (ldc <= 0) ldc = w->N;
     if (use_gemm(M))
-        return cuda_status(launch_gemm(w, static_cast<const uint8_t*>(ws), M, hi_prec, dC, w->N, dCS, stream));
+        return cuda_status(launch_gemm(w, static_cast<const uint8_t*>(ws), M, hi_prec, dC, ldc, dCS, stream));
     for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
         const ActView act = chunk_view(const_cast<void*>(ws), M, w->nblk, c, hi_prec);
         const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
-        cudaError_t e = launch_decode(w, act, hi_prec, dC ? dC + m0 * w->N : nullptr, w->N,
+        cudaError_t e = launch_decode(w, act, hi_prec, dC ? dC + m0 * ldc : nullptr, ldc,
                                       dCS ? dCS + m0 * w->N * w->nblk : nullptr, stream, pdl);
         if (e != cudaSuccess) return cuda_status(e);
     }
@@ -611,6 +615,18 @@ QL_API int ql_quantize_dev(const float* dA, int M, int K, uint8_t* dHi, uint8_t*
 // i4_matmul (kernel/quantized_matmul.cpp:526-552): host A[M,K] fp32 in, host
 // C[M,N] fp32 out, synchronous.  Like the reference it returns nothing; a
 // failure leaves C untouched and is reported by ql_last_status().
+// Output columns per chunk of the synchronous host-pointer call: outputs of at
+// least 2 chunks x 512 KB are split into up to 8 column chunks (multiples of
+// 128 columns, so every chunk is whole GEMM tiles and decode row groups); each
+// chunk's matmul runs on the call's stream and its device -> host copy starts
+// on a second stream as soon as it is done, overlapping the next chunk.
+static int output_chunks(int M, int N) {
+    const size_t bytes = static_cast<size_t>(M) * N * 4;
+    int chunks = static_cast<int>(std::min<size_t>(8, bytes / (512 * 1024)));
+    while (chunks > 1 && N / chunks < 128) --chunks;
+    return std::max(1, chunks);
+}
+
 QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
     if (!valid_weight(handle) || M < 0 || (M > 0 && (!A || !C))) {
         set_status(QL_EINVAL);
@@ -646,9 +662,47 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
         cuda_status(e);
         return;
     }
-    int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
+    const int chunks = output_chunks(M, w->N);
+    if (chunks == 1) {
+        int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
+        if (rc != QL_OK) return;
+        e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        cuda_status(e);
+        return;
+    }
+    if (!st->copy_stream) {
+        e = cudaStreamCreateWithFlags(&st->copy_stream, cudaStreamNonBlocking);
+        for (int i = 0; i < 8 && e == cudaSuccess; ++i)
+            e = cudaEventCreateWithFlags(&st->chunk_done[i], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            cuda_status(e);
+            return;
+        }
+    }
+    int rc = run_quantize(dA, M, w->K, ws, s, hp);
     if (rc != QL_OK) return;
-    e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    // column chunks of whole 128-column tiles; the last takes the remainder
+    const int per = ((w->N / chunks) / 128) * 128;
+    for (int i = 0; i < chunks && e == cudaSuccess; ++i) {
+        const int n0 = i * per;
+        const int nc = (i == chunks - 1) ? w->N - n0 : per;
+        Weight view = *w;                         // rows n0 .. n0+nc of the same records
+        view.N = nc;
+        view.G = nc / 16;
+        view.W = w->W + static_cast<size_t>(n0 / 16) * w->nblk * w->REC;
+        rc = run_compute(&view, ws, M, dC + n0, nullptr, s, hp, /*pdl=*/i == 0, /*ldc=*/w->N);
+        if (rc != QL_OK) break;
+        e = cudaEventRecord(st->chunk_done[i], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st->copy_stream, st->chunk_done[i], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(C + n0, static_cast<size_t>(w->N) * 4, dC + n0, static_cast<size_t>(w->N) * 4,
+                                  static_cast<size_t>(nc) * 4, M, cudaMemcpyDeviceToHost, st->copy_stream);
+    }
+    // both streams drain before returning (also after a failure, so no copy is in flight)
+    cudaError_t e1 = cudaStreamSynchronize(s);
+    cudaError_t e2 = cudaStreamSynchronize(st->copy_stream);
+    if (rc != QL_OK) return;
+    if (e == cudaSuccess) e = (e1 != cudaSuccess) ? e1 : e2;
     cuda_status(e);
 }

@@ -247,3 +247,24 @@ def test_full_size_sampled_columns(K, N, bits, M, oracle):
         expect = oracle.matmul(sub_qw, sub_sc, None, 16, K, bits, a)
         assert bits_equal(c[:, rows], expect), f"columns {16 * g}..{16 * g + 15}"
     assert np.isfinite(c).all()
+
+
+@pytest.mark.parametrize("M,N,K,bits", [(16, 16384, 256, 4), (64, 12288, 128, 8), (130, 4096, 256, 4),
+                                         (300, 2000, 224, 4), (9, 151936, 64, 8)])
+def test_host_call_output_chunks(M, N, K, bits):
+    """i4_matmul splits large outputs into column chunks whose device->host
+    copies overlap the next chunk's matmul; the result must be bit-identical to
+    the single device call (ql_matmul_dev_ws) for decode and prefill sizes,
+    ragged last chunks included."""
+    rng = np.random.default_rng(M + N)
+    nblk = K // 32
+    qw = rng.integers(0, 256, (N, nblk, 4 * bits), dtype=np.uint8)
+    sc = rng.uniform(1e-3, 2e-2, (N, nblk)).astype(np.float16)
+    h = qlc.prepack(qw, sc, None, N, K, bits)
+    qlc.set_hi_prec(True)
+    try:
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        assert bits_equal(qlc.matmul_host(h, a, N), qlc.matmul_dev(h, a, N))
+    finally:
+        qlc.set_hi_prec(False)
+        qlc.free(h)
