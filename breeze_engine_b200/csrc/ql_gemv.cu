@@ -254,6 +254,14 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
                 }
             }
             if (OUT_CS) continue;
+            // Every read of this stage's shared memory is done once the last
+            // sub-chunk's f values are in registers: hand the stage back to the
+            // producer before the (serial) relay wait and FFMA chain, so the
+            // ring refills while the chain runs.
+            if (j0 + C >= nb) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            }
             // ---- take the running accumulator of stage i-1 (once per stage)
             if (need_relay) {
                 need_relay = false;
@@ -278,10 +286,12 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
                 }
             }
         }
-        // release the stage to the producer
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-        if (OUT_CS) continue;
+        // release the stage to the producer (the FP32 path released it above)
+        if (OUT_CS) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            continue;
+        }
         if (p.SPLIT > 1 && i + 1 < nst) {
             // hand the accumulator to the warp of stage i + 1
             const int slot = i % NS;
