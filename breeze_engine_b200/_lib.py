@@ -44,6 +44,9 @@ SIGNATURES = [
     ("ql_act_workspace_bytes", _sz, [_i, _i]),
     ("ql_quantize_act_dev", _i, [_vp, _i, _i, _i, _vp, _sz, _vp]),
     ("ql_matmul_quantized_dev", _i, [_vp, _vp, _i, _i, _vp, _vp]),
+    ("ql_weight_serialized_bytes", _sz, [_vp]),
+    ("ql_weight_serialize", _i, [_vp, _vp, _sz]),
+    ("ql_weight_deserialize", _i, [_vp, _sz, ctypes.POINTER(_vp)]),
     ("ql_block_sums_dev", _i, [_vp, _vp, _i, _vp, _vp]),
     ("ql_quantize_dev", _i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
 ]

@@ -211,6 +211,36 @@ def _matmul_device(lib, handle, a, N, K, hdev, out=None, workspace=None):
     return out
 
 
+def save_packed(handle, path):
+    """Write a handle's packed device layout to ``path`` (a versioned header
+    plus the records), so a later :func:`load_packed` skips the MatMulNBits
+    repack.  The reference repacks on every load (``breeze/qwen35_cpu.py:71-89``)."""
+    lib = L.load()
+    n = lib.ql_weight_serialized_bytes(ctypes.c_void_p(handle))
+    if n == 0:
+        raise ValueError("invalid handle")
+    buf = np.empty(n, dtype=np.uint8)
+    L.check(lib.ql_weight_serialize(ctypes.c_void_p(handle), _p(buf), n), "save_packed")
+    with open(path, "wb") as f:
+        buf.tofile(f)
+    return n
+
+
+def load_packed(path):
+    """Create a handle on the current CUDA device from a file written by
+    :func:`save_packed`; ``ValueError`` for a corrupt or mismatched file."""
+    lib = L.load()
+    buf = np.fromfile(path, dtype=np.uint8)
+    out = ctypes.c_void_p()
+    rc = lib.ql_weight_deserialize(_p(buf), buf.size, ctypes.byref(out))
+    if rc == L.QL_EINVAL:
+        raise ValueError(f"{path}: not a packed weight of this library version (or corrupt)")
+    if rc == L.QL_ENOMEM or (rc == L.QL_OK and not out.value):
+        raise MemoryError(f"Could not allocate packed weights from {path}")
+    L.check(rc, "load_packed")
+    return out.value
+
+
 def free(handle):
     """Release a handle (``breeze/cpu_backend.py:240-242``); null-safe."""
     lib = L.try_load()

@@ -460,6 +460,99 @@ QL_API int ql_weight_info(const void* handle, int* N, int* K, int* bits, int* de
     return set_status(QL_OK);
 }
 
+// ------------------------------------------------------------------ packed-layout cache
+// A packed handle serialised to host bytes: a fixed header, then the device
+// records byte for byte.  Loading skips the MatMulNBits repack entirely (one
+// host -> device copy per weight).  The header pins the record geometry and
+// the library's layout version; a mismatch, a short buffer or a wrong payload
+// checksum is rejected with QL_EINVAL before any device memory is touched.
+namespace {
+constexpr char PACK_MAGIC[8] = {'Q', 'L', 'P', 'A', 'C', 'K', '1', 0};
+constexpr uint32_t PACK_VERSION = 1;     // record layout of ql_internal.h
+struct PackHeader {
+    char magic[8];
+    uint32_t version, header_bytes;
+    int32_t N, K, bits, scale_half, has_zp, REC;
+    uint64_t payload_bytes;              // G * nblk * REC
+    uint64_t checksum;                   // wrapping sum of the payload's 64-bit words (x odd index weights)
+};
+static_assert(sizeof(PackHeader) == 56, "packed-layout header");
+
+uint64_t payload_checksum(const uint8_t* p, size_t n) {
+    uint64_t sum = 0x9E3779B97F4A7C15ull;
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+        uint64_t v;
+        std::memcpy(&v, p + i, 8);
+        sum += v * (2 * (i >> 3) + 1);
+    }
+    for (; i < n; ++i) sum += static_cast<uint64_t>(p[i]) << ((i & 7) * 8);
+    return sum;
+}
+}  // namespace
+
+QL_API size_t ql_weight_serialized_bytes(const void* handle) {
+    if (!valid_weight(handle)) return 0;
+    const auto* w = static_cast<const Weight*>(handle);
+    return sizeof(PackHeader) + static_cast<size_t>(w->G) * w->nblk * w->REC;
+}
+
+QL_API int ql_weight_serialize(const void* handle, void* host_buf, size_t bytes) {
+    if (!valid_weight(handle) || !host_buf) return set_status(QL_EINVAL);
+    const auto* w = static_cast<const Weight*>(handle);
+    const size_t payload = static_cast<size_t>(w->G) * w->nblk * w->REC;
+    if (bytes < sizeof(PackHeader) + payload) return set_status(QL_EINVAL);
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return set_status(QL_ECUDA);
+    uint8_t* out = static_cast<uint8_t*>(host_buf);
+    cudaError_t e = cudaMemcpy(out + sizeof(PackHeader), w->W, payload, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_status(e);
+    PackHeader h{};
+    std::memcpy(h.magic, PACK_MAGIC, 8);
+    h.version = PACK_VERSION;
+    h.header_bytes = sizeof(PackHeader);
+    h.N = w->N;
+    h.K = w->K;
+    h.bits = w->bits;
+    h.scale_half = w->scale_half;
+    h.has_zp = w->has_zp;
+    h.REC = w->REC;
+    h.payload_bytes = payload;
+    h.checksum = payload_checksum(out + sizeof(PackHeader), payload);
+    std::memcpy(out, &h, sizeof(h));
+    return set_status(QL_OK);
+}
+
+QL_API int ql_weight_deserialize(const void* host_buf, size_t bytes, void** out_handle) {
+    if (!out_handle) return set_status(QL_EINVAL);
+    *out_handle = nullptr;
+    if (!host_buf || bytes < sizeof(PackHeader)) return set_status(QL_EINVAL);
+    PackHeader h;
+    std::memcpy(&h, host_buf, sizeof(h));
+    if (std::memcmp(h.magic, PACK_MAGIC, 8) != 0 || h.version != PACK_VERSION ||
+        h.header_bytes != sizeof(PackHeader))
+        return set_status(QL_EINVAL);
+    if (h.N <= 0 || h.K <= 0 || h.N % 16 || h.K % 32 || (h.bits != 4 && h.bits != 8) ||
+        (h.scale_half != 0 && h.scale_half != 1) || (h.has_zp != 0 && h.has_zp != 1) || (h.bits == 8 && h.has_zp))
+        return set_status(QL_EINVAL);
+    int TB, SB, ZB, REC;
+    weight_geometry(h.bits, h.scale_half != 0, h.has_zp != 0, &TB, &SB, &ZB, &REC);
+    const size_t payload = static_cast<size_t>(h.N / 16) * (h.K / 32) * REC;
+    if (h.REC != REC || h.payload_bytes != payload || bytes < sizeof(PackHeader) + payload)
+        return set_status(QL_EINVAL);
+    const uint8_t* src = static_cast<const uint8_t*>(host_buf) + sizeof(PackHeader);
+    if (payload_checksum(src, payload) != h.checksum) return set_status(QL_EINVAL);
+    Weight* w = allocate_weight(h.N, h.K, h.bits, h.scale_half, h.has_zp);
+    if (!w) return set_status(QL_ENOMEM);
+    cudaError_t e = cudaMemcpy(w->W, src, payload, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_status(e);
+    }
+    *out_handle = w;
+    return set_status(QL_OK);
+}
+
 // ------------------------------------------------------------------ matmul
 
 // Workspace bytes ql_matmul_dev_ws needs for M rows (0 for M <= 0).

@@ -168,6 +168,19 @@ int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, fl
  * Same numerics and arguments as ql_matmul_dev. */
 int ql_matmul_dev_noalloc(void* handle, const float* dA, int M, float* dC, void* stream);
 
+/* Packed-layout cache (no counterpart in the reference, which repacks every
+ * MatMulNBits weight on each load, breeze/qwen35_cpu.py:71-89 ->
+ * kernel/quantized_matmul.cpp:505-520; the survey's next step for 27B loads).
+ * ql_weight_serialized_bytes: size of the serialised form of a handle (0 for
+ * an invalid handle).  ql_weight_serialize: writes a versioned header and the
+ * handle's device records into host_buf (>= that many bytes).
+ * ql_weight_deserialize: checks the header, sizes and payload checksum
+ * (QL_EINVAL on any mismatch, before touching device memory) and creates a new
+ * handle on the current device with one host -> device copy. */
+size_t ql_weight_serialized_bytes(const void* handle);
+int ql_weight_serialize(const void* handle, void* host_buf, size_t bytes);
+int ql_weight_deserialize(const void* host_buf, size_t bytes, void** out_handle);
+
 /* The per-block INT32 accumulators cs[M][N][K/32] = sum_k q16*(w-zp) of the
  * reference's tile_kernel (kernel/quantized_matmul.cpp:298-312, 262-268),
  * produced by this library's own integer MMA path (INT32 parity checks). */
