@@ -176,16 +176,24 @@ class Layer:
     """One packed weight (possibly several rotation copies) of a (K, N) layer shard.
 
     ``mode='col'``: rank r keeps output rows [r N/P, (r+1) N/P) (column-parallel);
-    ``mode='row'``: rank r keeps input blocks [r K/P, (r+1) K/P) (row-parallel)."""
+    ``mode='row'``: rank r keeps input blocks [r K/P, (r+1) K/P) (row-parallel);
+    ``mode='whole'``: the full layer, packed only where ``build`` is true (the
+    ranks that run one of its calls)."""
 
-    def __init__(self, lib, K, N, bits, world, rank, seed, copies, mode="col"):
+    def __init__(self, lib, K, N, bits, world, rank, seed, copies, mode="col", build=True):
         import torch
         from breeze_engine_b200 import backend
         from breeze_engine_b200.quant import quantize_matmul_nbits_torch
         self.K, self.N, self.bits, self.mode = K, N, bits, mode
-        self.n_local = N // world if mode == "col" else N
-        self.k_local = K if mode == "col" else K // world
-        self.k0 = 0 if mode == "col" else rank * self.k_local
+        if mode == "whole":
+            world, rank = 1, 0
+        self.n_local = N // world if mode != "row" else N
+        self.k_local = K if mode != "row" else K // world
+        self.k0 = 0 if mode != "row" else rank * self.k_local
+        self.handles = []
+        self.shard_bytes = self.n_local * self.k_local * bits // 8 + 2 * self.n_local * (self.k_local // 32)
+        if not build:
+            return
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
         w = torch.randn((K, N), generator=g, device="cuda", dtype=torch.float32).mul_(0.02)
@@ -196,12 +204,11 @@ class Layer:
             n0 = rank * self.n_local
             qw = qw[n0:n0 + self.n_local].contiguous()
             sc = sc.reshape(N, nblk)[n0:n0 + self.n_local].contiguous()
-        else:
+        elif mode == "row":
             b0, nb = self.k0 // 32, self.k_local // 32
             qw = qw.reshape(N, nblk, -1)[:, b0:b0 + nb].contiguous()
             sc = sc.reshape(N, nblk)[:, b0:b0 + nb].contiguous()
         self.handles = [backend.prepack(qw, sc, None, self.k_local, self.n_local, bits) for _ in range(copies)]
-        self.shard_bytes = self.n_local * self.k_local * bits // 8 + 2 * self.n_local * (self.k_local // 32)
         del qw, sc
         torch.cuda.empty_cache()
 
@@ -234,13 +241,33 @@ class DecodeWorkload:
     bits = 8
     kernel = "decode_kernel (ql_gemv.cu)"
 
+    # Layers of at least this many weight bytes are column-sharded across the
+    # GPUs (NCCL all-gather of the outputs); smaller layers stay whole and their
+    # calls -- independent units of the sweep -- are dealt round-robin to the
+    # GPUs, so only sharded shapes have a collective.
+    SHARD_BYTES = 256 << 20
+
     def build(self, lib, world, rank):
         import torch
         layers = []
+        self.owners = {}
+        small = 0
         for i, (K, N) in enumerate(self.shapes):
-            shard = (N // world) * K + 2 * (N // world) * (K // 32)
-            copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
-            layers.append(Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies))
+            whole = world > 1 and N * K * self.bits // 8 < self.SHARD_BYTES
+            if whole:
+                owners = [(small + j) % world for j in range(len(self.Ms))]
+                small += len(self.Ms)
+                shard = N * K
+                copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
+                layer = Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies, mode="whole",
+                              build=rank in owners)
+                for M, o in zip(self.Ms, owners):
+                    self.owners[(id(layer), M)] = o
+            else:
+                shard = (N // world) * K + 2 * (N // world) * (K // 32)
+                copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
+                layer = Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies)
+            layers.append(layer)
         g = torch.Generator(device="cuda")
         g.manual_seed(7)
         acts = {}
@@ -250,7 +277,8 @@ class DecodeWorkload:
         calls = []
         for layer in layers:
             for j, M in enumerate(self.Ms):
-                calls.append((layer, layer.handles[j % len(layer.handles)], M))
+                h = layer.handles[j % len(layer.handles)] if layer.handles else None
+                calls.append((layer, h, M))
         return layers, acts, calls
 
     def step_amount(self, calls):
@@ -281,7 +309,9 @@ class DecodeWorkload:
                 "activations": "two-pass INT16 (hi_prec=1)",
                 "l2": "rotated weight copies; step working set > L2",
                 "timing": "CUDA graph of one step (12 quantize+matmul calls), CUDA events",
-                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+                "parallelism": ("1 GPU" if world == 1 else
+                                f"LM head (661 MB) column-parallel N/{world} + NCCL all-gather; the 50 MB "
+                                f"layers whole, their 8 calls dealt round-robin over the {world} GPUs")}
 
     def cpu_calls(self):
         """(K, N, bits, Ms) of the reference timing; `samples` steps of these."""
@@ -477,8 +507,17 @@ def run_ours(args):
     backend.set_hi_prec(True)
 
     layers, acts, calls = wl.build(lib, world, rank)
+    owners = getattr(wl, "owners", {})
+
+    def mine(layer, M):
+        """Whether this rank runs the call: every rank for sharded layers, the
+        owner for whole layers dealt to one GPU."""
+        return layer.mode != "whole" or owners.get((id(layer), M)) == rank
+
     outs, wss, local_a = {}, {}, {}
     for layer, h, M in calls:
+        if not mine(layer, M):
+            continue
         outs[(id(layer), M)] = torch.empty((M, layer.n_local), dtype=torch.float32, device="cuda")
         need = lib.ql_workspace_bytes(ctypes.c_void_p(h), M)
         if (layer.k_local, M) not in wss or wss[(layer.k_local, M)].numel() < need:
@@ -490,6 +529,8 @@ def run_ours(args):
     def step():
         s_ptr = torch.cuda.current_stream().cuda_stream
         for layer, h, M in calls:
+            if not mine(layer, M):
+                continue
             a, c, ws = local_a[(id(layer), M)], outs[(id(layer), M)], wss[(layer.k_local, M)]
             if layer.mode == "row":
                 a.copy_(acts[(M, layer.K)][:, layer.k0:layer.k0 + layer.k_local])
@@ -500,7 +541,7 @@ def run_ours(args):
             if world > 1:
                 if layer.mode == "col":
                     gather_columns(c)
-                else:
+                elif layer.mode == "row":
                     reduce_partials(c, "scatter")
 
     def barrier():
@@ -528,18 +569,20 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def timed_replays(g, n, label="bench"):
+        """Device time of n replays of graph g, max over ranks; a rank with no
+        graph (a call another GPU owns) takes part in the barriers with 0."""
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push(label)          # lets ncu --nvtx restrict a capture to it
         e0.record(stream)
-        for _ in range(n):
+        for _ in range(n if g is not None else 0):
             g.replay()
         e1.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
-        return max_over_ranks(e0.elapsed_time(e1) / 1e3)
+        return max_over_ranks(e0.elapsed_time(e1) / 1e3 if g is not None else 0.0)
 
     for _ in range(args.warmup):
         graph.replay()
@@ -564,7 +607,7 @@ def run_ours(args):
     qws = {}
     for layer, h, M in calls:
         key = (id(layer), M)
-        if key not in qws:
+        if key not in qws and mine(layer, M):
             a = local_a[key]
             if layer.mode == "row":
                 a.copy_(acts[(M, layer.K)][:, layer.k0:layer.k0 + layer.k_local])
@@ -577,15 +620,17 @@ def run_ours(args):
     REPS = 8 if wl.name == "decode" else 4
     kern_t, kern_amount, per_call = 0.0, 0, []
     for layer, h0, M in calls:
-        c, ws = outs[(id(layer), M)], qws[(id(layer), M)]
-        gk = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gk):
-            s_ptr = torch.cuda.current_stream().cuda_stream
-            for r in range(REPS):
-                h = layer.handles[(layer.handles.index(h0) + r) % len(layer.handles)]
-                rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s_ptr)
-                assert rc == 0
-        gk.replay()
+        gk = None
+        if mine(layer, M):
+            c, ws = outs[(id(layer), M)], qws[(id(layer), M)]
+            gk = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gk):
+                s_ptr = torch.cuda.current_stream().cuda_stream
+                for r in range(REPS):
+                    h = layer.handles[(layer.handles.index(h0) + r) % len(layer.handles)]
+                    rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s_ptr)
+                    assert rc == 0
+            gk.replay()
         nrep = max(2, args.steps // 2)
         dt = timed_replays(gk, nrep) / (nrep * REPS)
         amt = wl.kernel_amount(M, layer.k_local, layer.n_local, layer.bits)
@@ -607,6 +652,8 @@ def run_ours(args):
 
         def e2e_step():
             for layer, h, M in calls:
+                if not mine(layer, M):
+                    continue
                 a = host_a[(id(layer), M)]
                 c = host_c[(id(layer), M)]
                 lib.i4_matmul(ctypes.c_void_p(h), ctypes.c_void_p(a.data_ptr()), M, ctypes.c_void_p(c.data_ptr()))
@@ -638,7 +685,7 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
             "config": wl.config(world),
             "roofline": roofline,
-            "gpu_launches": 2 * len(calls) * args.steps,
+            "gpu_launches": 2 * sum(1 for layer, _, M in calls if mine(layer, M)) * args.steps,
             "clocks": clock_info,
         }
         if e2e:
