@@ -247,16 +247,26 @@ class DecodeWorkload:
     # GPUs, so only sharded shapes have a collective.
     SHARD_BYTES = 256 << 20
 
+    @classmethod
+    def plan(cls, world):
+        """Per shape: ("col", None) -- column-sharded over all GPUs -- or
+        ("whole", owners) with the owning GPU of each of its calls (one per M),
+        dealt round-robin over the small layers' calls."""
+        out, small = [], 0
+        for K, N in cls.shapes:
+            if world > 1 and N * K * cls.bits // 8 < cls.SHARD_BYTES:
+                out.append(("whole", [(small + j) % world for j in range(len(cls.Ms))]))
+                small += len(cls.Ms)
+            else:
+                out.append(("col", None))
+        return out
+
     def build(self, lib, world, rank):
         import torch
         layers = []
         self.owners = {}
-        small = 0
-        for i, (K, N) in enumerate(self.shapes):
-            whole = world > 1 and N * K * self.bits // 8 < self.SHARD_BYTES
-            if whole:
-                owners = [(small + j) % world for j in range(len(self.Ms))]
-                small += len(self.Ms)
+        for i, ((K, N), (mode, owners)) in enumerate(zip(self.shapes, self.plan(world))):
+            if mode == "whole":
                 shard = N * K
                 copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
                 layer = Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies, mode="whole",
