@@ -44,6 +44,10 @@ SIGNATURES = [
     ("ql_act_workspace_bytes", _sz, [_i, _i]),
     ("ql_quantize_act_dev", _i, [_vp, _i, _i, _i, _vp, _sz, _vp]),
     ("ql_matmul_quantized_dev", _i, [_vp, _vp, _i, _i, _vp, _vp]),
+    ("ql_norm_act_workspace_bytes", _sz, [_i, _i]),
+    ("ql_quantize_act_rmsnorm_dev", _i, [_vp, _vp, ctypes.c_float, _i, _i, _i, _vp, _sz, _vp, _vp]),
+    ("ql_matmul_rmsnorm_dev", _i, [_vp, _vp, _vp, ctypes.c_float, _i, _vp, _vp]),
+    ("ql_weight_concat", _i, [ctypes.POINTER(_vp), _i, ctypes.POINTER(_vp)]),
     ("ql_weight_serialized_bytes", _sz, [_vp]),
     ("ql_weight_serialize", _i, [_vp, _vp, _sz]),
     ("ql_weight_deserialize", _i, [_vp, _sz, ctypes.POINTER(_vp)]),

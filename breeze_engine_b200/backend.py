@@ -211,6 +211,67 @@ def _matmul_device(lib, handle, a, N, K, hdev, out=None, workspace=None):
     return out
 
 
+def rmsnorm_matmul(handle, x, norm_w, eps, N, out=None):
+    """``matmul(rmsnorm(x, norm_w, eps))`` with the normalisation fused into
+    the activation quantizer: the reference decoder's ``rmsnorm`` followed by
+    ``i4_matmul`` on its output (``kernel/qwen35_decoder.cpp:133-141``, then
+    ``:329``, ``:395``, ``:406-407``, ``:421``), bit for bit.  ``x`` fp32
+    ``[M, K]`` and ``norm_w`` fp32 ``[K]`` are CUDA tensors on the handle's
+    device; asynchronous on the current stream.  The activation mode is the
+    process-wide one (:func:`set_hi_prec`)."""
+    lib = L.load()
+    torch = _torch()
+    hN, hK, _, hdev, _ = weight_info(handle)
+    if int(N) != hN:
+        raise ValueError(f"N={N} does not match the packed weight (N={hN})")
+    if not (_is_cuda_tensor(x) and _is_cuda_tensor(norm_w)):
+        raise TypeError("rmsnorm_matmul takes CUDA tensors")
+    if x.dim() != 2 or x.shape[1] != hK or tuple(norm_w.shape) != (hK,):
+        raise ValueError(f"x must be [M, {hK}] and norm_w [{hK}]")
+    if x.device.index != hdev or norm_w.device.index != hdev:
+        raise ValueError(f"inputs must be on cuda:{hdev}, where the weights are")
+    x = x.to(torch.float32).contiguous()
+    norm_w = norm_w.to(torch.float32).contiguous()
+    if x.data_ptr() % 16:
+        x = x.clone()
+    if norm_w.data_ptr() % 16:
+        norm_w = norm_w.clone()
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, hN), dtype=torch.float32, device=x.device)
+    if M == 0:
+        return out
+    hp = get_hi_prec()
+    need = lib.ql_norm_act_workspace_bytes(int(M), int(hK))
+    ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        L.check(lib.ql_quantize_act_rmsnorm_dev(x.data_ptr(), norm_w.data_ptr(), float(eps), int(M), int(hK),
+                                                int(hp), ws.data_ptr(), need, None, stream), "rmsnorm_matmul")
+        L.check(lib.ql_matmul_quantized_dev(ctypes.c_void_p(handle), ws.data_ptr(), int(M), int(hp),
+                                            out.data_ptr(), stream), "rmsnorm_matmul")
+    return out
+
+
+def concat_packed(handles):
+    """One new handle stacking ``handles`` along N (same K, bits, scale type
+    and zero points), e.g. gate and up, so projections that share an input run
+    as one launch (the reference calls ``i4_matmul`` once per projection,
+    ``kernel/qwen35_decoder.cpp:406-407``).  Output columns follow the order
+    given; the sources stay valid and are freed separately."""
+    lib = L.load()
+    handles = list(handles)
+    if not handles:
+        raise ValueError("concat_packed needs at least one handle")
+    arr = (ctypes.c_void_p * len(handles))(*handles)
+    out = ctypes.c_void_p()
+    rc = lib.ql_weight_concat(arr, len(handles), ctypes.byref(out))
+    if rc == L.QL_EINVAL:
+        raise ValueError("handles differ in K, bits, scale type, zero points or device")
+    L.check(rc, "concat_packed")
+    return out.value
+
+
 def save_packed(handle, path):
     """Write a handle's packed device layout to ``path`` (a versioned header
     plus the records), so a later :func:`load_packed` skips the MatMulNBits

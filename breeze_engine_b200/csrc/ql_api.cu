@@ -633,6 +633,131 @@ QL_API int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_p
     return run_compute(w, ws, M, dC, nullptr, static_cast<cudaStream_t>(stream), hi_prec != 0, true);
 }
 
+// ------------------------------------------------------------------ fused RMSNorm prologue
+//
+// The reference decoder runs rmsnorm into a scratch row and then i4_matmul on
+// it (kernel/qwen35_decoder.cpp:133-141, 405-407), which re-reads the row to
+// quantize it.  Here the row factors are computed once (ql_norm.cu) and the
+// quantizer applies x * inv * w while it loads the row, so the normalised
+// activations never round-trip through memory unless the caller asks for them.
+// Workspace: the quantized activations, then M fp32 row factors.
+namespace {
+size_t norm_ws_bytes(int M, int nblk) {
+    return align256(ws_bytes_for(M, nblk)) + align256(static_cast<size_t>(M) * sizeof(float));
+}
+
+int run_quantize_norm(const float* dX, const float* dW, float eps, int M, int K, void* ws, float* dHn,
+                      cudaStream_t stream, bool hi_prec) {
+    const int nblk = K / 32;
+    float* row_inv = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256(ws_bytes_for(M, nblk)));
+    cudaError_t e = launch_rmsnorm_factors(dX, K, M, K, eps, row_inv, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (use_gemm(M)) {
+        const NormArgs n{row_inv, dW, dHn, K};
+        return cuda_status(launch_quantize_gemm(dX, K, M, K, hi_prec, static_cast<uint8_t*>(ws), stream, &n));
+    }
+    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
+        const ActView act = chunk_view(ws, M, nblk, c, hi_prec);
+        const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
+        const NormArgs n{row_inv + m0, dW, dHn ? dHn + m0 * K : nullptr, K};
+        e = launch_quantize_act(dX + m0 * K, K, act.M, K, hi_prec, act, stream, &n);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    return set_status(QL_OK);
+}
+
+int check_norm_args(const float* dX, const float* dW, int M, int K, const float* dHn) {
+    if (M < 0 || K <= 0 || K % 32) return QL_EINVAL;
+    if (M == 0) return QL_OK;
+    if (!dX || !dW) return QL_EINVAL;
+    if (reinterpret_cast<uintptr_t>(dX) % 16 || reinterpret_cast<uintptr_t>(dW) % 16 ||
+        reinterpret_cast<uintptr_t>(dHn) % 16)
+        return QL_EINVAL;        // 16-byte vector loads and stores
+    return QL_OK;
+}
+}  // namespace
+
+QL_API size_t ql_norm_act_workspace_bytes(int M, int K) {
+    if (M <= 0 || K <= 0 || K % 32) return 0;
+    return norm_ws_bytes(M, K / 32);
+}
+
+QL_API int ql_quantize_act_rmsnorm_dev(const float* dX, const float* dNormW, float eps, int M, int K,
+                                       int hi_prec, void* ws, size_t ws_bytes, float* dHn, void* stream) {
+    const int c = check_norm_args(dX, dNormW, M, K, dHn);
+    if (c != QL_OK || M == 0) return set_status(c);
+    if (!ws || reinterpret_cast<uintptr_t>(ws) % 16 || ws_bytes < norm_ws_bytes(M, K / 32))
+        return set_status(QL_EINVAL);
+    return run_quantize_norm(dX, dNormW, eps, M, K, ws, dHn, static_cast<cudaStream_t>(stream), hi_prec != 0);
+}
+
+QL_API int ql_matmul_rmsnorm_dev(void* handle, const float* dX, const float* dNormW, float eps, int M,
+                                 float* dC, void* stream) {
+    int c = check_call(handle, dX, M, dC);
+    if (c != QL_OK || M == 0) return set_status(c);
+    const auto* w = static_cast<const Weight*>(handle);
+    c = check_norm_args(dX, dNormW, M, w->K, nullptr);
+    if (c != QL_OK) return set_status(c);
+    const bool hp = ql_get_hi_prec() != 0;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* st = state_for(w->device);
+    cudaError_t e = ensure(&st->ws, &st->ws_bytes, norm_ws_bytes(M, w->nblk));
+    if (e != cudaSuccess) return cuda_status(e);
+    const int rc = run_quantize_norm(dX, dNormW, eps, M, w->K, st->ws, nullptr, s, hp);
+    if (rc != QL_OK) return rc;
+    return run_compute(w, st->ws, M, dC, nullptr, s, hp, /*pdl=*/true);
+}
+
+// ------------------------------------------------------------------ concatenated weights
+//
+// Records are laid out row group by row group (rec[G][nblk][REC]), so stacking
+// weights along N is a byte concatenation of their record arrays.  One handle
+// over [gate; up] runs both projections that share an input in one launch
+// (kernel/qwen35_decoder.cpp:406-407 makes two i4_matmul calls).
+QL_API int ql_weight_concat(void* const* handles, int count, void** out_handle) {
+    if (!out_handle) return set_status(QL_EINVAL);
+    *out_handle = nullptr;
+    if (!handles || count <= 0) return set_status(QL_EINVAL);
+    if (!valid_weight(handles[0])) return set_status(QL_EINVAL);
+    const auto* first = static_cast<const Weight*>(handles[0]);
+    long long total_n = 0;
+    for (int i = 0; i < count; ++i) {
+        if (!valid_weight(handles[i])) return set_status(QL_EINVAL);
+        const auto* h = static_cast<const Weight*>(handles[i]);
+        if (h->K != first->K || h->bits != first->bits || h->scale_half != first->scale_half ||
+            h->has_zp != first->has_zp || h->device != first->device)
+            return set_status(QL_EINVAL);
+        total_n += h->N;
+    }
+    if (total_n > (1LL << 30)) return set_status(QL_EINVAL);
+    DeviceGuard guard(first->device);
+    if (!guard.ok) return set_status(QL_ECUDA);
+    Weight* w = allocate_weight(static_cast<int>(total_n), first->K, first->bits, first->scale_half,
+                                first->has_zp);
+    if (!w) return set_status(QL_ENOMEM);
+    cudaStream_t s = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        s = internal_stream(state_for(first->device));
+    }
+    size_t off = 0;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < count && e == cudaSuccess; ++i) {
+        const auto* h = static_cast<const Weight*>(handles[i]);
+        const size_t n = static_cast<size_t>(h->G) * h->nblk * h->REC;
+        e = cudaMemcpyAsync(w->W + off, h->W, n, cudaMemcpyDeviceToDevice, s);
+        off += n;
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        free_weight(w);
+        return cuda_status(e);
+    }
+    *out_handle = w;
+    return set_status(QL_OK);
+}
+
 // ------------------------------------------------------------------ no-allocation variant
 //
 // Some callers cannot allocate device memory at the time they run a layer:

@@ -71,6 +71,20 @@ struct ActView {
 size_t act_bytes(int M, int nblk);                       // one chunk of M <= 64 tokens
 ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 
+// Optional RMSNorm prologue of the activation quantizers (the reference
+// decoder's rmsnorm before its projections, kernel/qwen35_decoder.cpp:133-141):
+// the value quantized for (m, k) is (x[m][k] * row_inv[m]) * w[k], two rounded
+// fp32 products in that order, and hn (if set) receives it.
+struct NormArgs {
+    const float* row_inv;   // [M] 1/sqrt(mean(x^2) + eps), from launch_rmsnorm_factors
+    const float* w;         // [K] norm weights
+    float* hn;              // [M][ldh] normalised rows, or nullptr
+    int ldh;
+};
+// row_inv[m] for M rows of X (ldx floats apart, K wide), ql_norm.cu.
+cudaError_t launch_rmsnorm_factors(const float* X, int ldx, int M, int K, float eps, float* row_inv,
+                                   cudaStream_t stream);
+
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 
 // Prefill (M > MAX_DECODE_TOKENS) runs the tcgen05 GEMMs (ql_gemm16.cu,
@@ -95,7 +109,7 @@ __host__ __device__ inline size_t gemm_scales_off(int mt, int b, int m_tiles, in
 }
 size_t gemm_act_bytes(int M, int nblk);
 cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, const NormArgs* norm = nullptr);
 cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec, float* C, int ldc,
                         int32_t* cs, cudaStream_t stream);
 
@@ -114,7 +128,7 @@ constexpr size_t QL_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
-                                const ActView& out, cudaStream_t stream);
+                                const ActView& out, cudaStream_t stream, const NormArgs* norm = nullptr);
 cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,
                                 float* ascale, cudaStream_t stream);
 cudaError_t launch_decode(const Weight* w, const ActView& act, bool hi_prec, float* C,

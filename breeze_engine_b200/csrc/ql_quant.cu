@@ -26,9 +26,41 @@ __device__ __forceinline__ int to_int_like_lrint(float x) {
     return 0;   // NaN, +-inf, |x| >= 2^63
 }
 
-template <bool HP>
+// The 32 values of (token m, block b): row m of A itself or, with the RMSNorm
+// prologue (NORM), a = (x * row_inv[m]) * w[k] as the reference decoder's
+// rmsnorm writes them (kernel/qwen35_decoder.cpp:139: x * inv * w, evaluated
+// left to right, each product rounded to fp32), stored to hn when it is set.
+template <bool NORM>
+__device__ __forceinline__ void load_block(const float* __restrict__ A, int lda, int m, int b,
+                                           const NormArgs& nrm, float (&v)[32]) {
+    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = __ldg(src + i);
+        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    if (NORM) {
+        const float r = __ldg(nrm.row_inv + m);
+        const float4* w4 = reinterpret_cast<const float4*>(nrm.w + b * BLOCK_K);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 g = __ldg(w4 + i);
+            v[4 * i + 0] = __fmul_rn(__fmul_rn(v[4 * i + 0], r), g.x);
+            v[4 * i + 1] = __fmul_rn(__fmul_rn(v[4 * i + 1], r), g.y);
+            v[4 * i + 2] = __fmul_rn(__fmul_rn(v[4 * i + 2], r), g.z);
+            v[4 * i + 3] = __fmul_rn(__fmul_rn(v[4 * i + 3], r), g.w);
+        }
+        if (nrm.hn) {
+            float4* dst = reinterpret_cast<float4*>(nrm.hn + static_cast<size_t>(m) * nrm.ldh + b * BLOCK_K);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    }
+}
+
+template <bool HP, bool NORM>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ A, int lda,
-                                                           int M, int K, ActView out) {
+                                                           int M, int K, ActView out, NormArgs nrm) {
     // Let a dependent (PDL) kernel start its weight streaming right away; it
     // still waits for this grid's completion before reading the planes.  This
     // grid itself may have started before its predecessor finished (it is
@@ -60,13 +92,8 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
         return;
     }
 
-    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
     float v[32];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 f = __ldg(src + i);
-        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
+    load_block<NORM>(A, lda, m, b, nrm, v);
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -111,9 +138,9 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
 // s8; q8 in single-pass mode) and the lo plane (u8) as canonical K-major
 // tcgen05 B operands [2 K halves][8 groups of 8 tokens][8 tokens x 16 B], and
 // per (128-token tile, block) 128 fp32 scales.  Tokens M..(tile end) are zeros.
-template <bool HP>
+template <bool HP, bool NORM>
 __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restrict__ A, int lda, int M, int K,
-                                                            int m_tiles, uint8_t* __restrict__ out) {
+                                                            int m_tiles, uint8_t* __restrict__ out, NormArgs nrm) {
     pdl_launch_dependents();
     pdl_wait();                 // launched with PDL: the predecessor may still run
     const int nblk = K / BLOCK_K;
@@ -134,13 +161,8 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
         *scale = 0.0f;
         return;
     }
-    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
     float v[32];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 f = __ldg(src + i);
-        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
+    load_block<NORM>(A, lda, m, b, nrm, v);
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -197,13 +219,18 @@ static cudaError_t launch_pdl(void (*kern)(Args...), unsigned grid, unsigned thr
 }
 
 cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, const NormArgs* norm) {
     const int m_tiles = (M + 127) / 128;
     const long long total = static_cast<long long>(m_tiles) * 128 * (K / BLOCK_K);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-    if (hi_prec) return launch_pdl(quantize_gemm_kernel<true>, grid, threads, stream, A, lda, M, K, m_tiles, out);
-    return launch_pdl(quantize_gemm_kernel<false>, grid, threads, stream, A, lda, M, K, m_tiles, out);
+    const NormArgs n = norm ? *norm : NormArgs{};
+    if (norm) {
+        if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, true>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+        return launch_pdl(quantize_gemm_kernel<false, true>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+    }
+    if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, false>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+    return launch_pdl(quantize_gemm_kernel<false, false>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
 }
 
 // Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
@@ -265,12 +292,17 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec) {
 }
 
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
-                                const ActView& out, cudaStream_t stream) {
+                                const ActView& out, cudaStream_t stream, const NormArgs* norm) {
     const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-    if (hi_prec) return launch_pdl(quantize_act_kernel<true>, grid, threads, stream, A, lda, M, K, out);
-    return launch_pdl(quantize_act_kernel<false>, grid, threads, stream, A, lda, M, K, out);
+    const NormArgs n = norm ? *norm : NormArgs{};
+    if (norm) {
+        if (hi_prec) return launch_pdl(quantize_act_kernel<true, true>, grid, threads, stream, A, lda, M, K, out, n);
+        return launch_pdl(quantize_act_kernel<false, true>, grid, threads, stream, A, lda, M, K, out, n);
+    }
+    if (hi_prec) return launch_pdl(quantize_act_kernel<true, false>, grid, threads, stream, A, lda, M, K, out, n);
+    return launch_pdl(quantize_act_kernel<false, false>, grid, threads, stream, A, lda, M, K, out, n);
 }
 
 cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,

@@ -153,6 +153,35 @@ int ql_quantize_act_dev(const float* dA, int M, int K, int hi_prec, void* ws, si
 int ql_matmul_quantized_dev(void* handle, const void* ws, int M, int hi_prec, float* dC,
                             void* stream);
 
+/* Fused RMSNorm prologue (no counterpart in the reference's C ABI; it
+ * replaces the reference decoder's rmsnorm-then-i4_matmul pair,
+ * kernel/qwen35_decoder.cpp:133-141 followed by :329/:395/:406-407/:421):
+ * the activations quantized are hn = rmsnorm(dX, dNormW, eps) row by row,
+ *   inv = 1.0f / sqrtf((float)(sum_j (double)x_j^2 / K) + eps),  hn_j = x_j * inv * w_j,
+ * bit-identical to the reference's serial double sum and fp32 products, so
+ * the result equals i4_matmul(handle, hn, M, C) on the reference's own hn.
+ * ql_quantize_act_rmsnorm_dev: the split form of ql_quantize_act_dev (then
+ * ql_matmul_quantized_dev, once per weight sharing the normalised input);
+ * its workspace is >= ql_norm_act_workspace_bytes(M, K) bytes (the quantized
+ * activations plus M row factors); dHn (16-byte aligned, may be NULL)
+ * receives hn [M,K].  ql_matmul_rmsnorm_dev: one call with the library's
+ * workspace and the process-wide activation mode (i4_set_hi_prec).  dX and
+ * dNormW are 16-byte aligned device pointers, K % 32 == 0. */
+size_t ql_norm_act_workspace_bytes(int M, int K);
+int ql_quantize_act_rmsnorm_dev(const float* dX, const float* dNormW, float eps, int M, int K,
+                                int hi_prec, void* ws, size_t ws_bytes, float* dHn, void* stream);
+int ql_matmul_rmsnorm_dev(void* handle, const float* dX, const float* dNormW, float eps, int M,
+                          float* dC, void* stream);
+
+/* One handle stacking `count` weights along N (no counterpart in the
+ * reference, which calls i4_matmul once per projection that shares an input,
+ * e.g. gate and up at kernel/qwen35_decoder.cpp:406-407).  All handles need
+ * the same K, bits, scale type, zero-point presence and device (QL_EINVAL
+ * otherwise); output columns follow the handles' order.  Results are those
+ * of the separate weights, bit for bit.  The sources stay valid; finish any
+ * ql_prepack_onnx_dev writing them before the call.  Free with i4_free. */
+int ql_weight_concat(void* const* handles, int count, void** out_handle);
+
 /* ql_matmul_dev without any device allocation (no counterpart in the
  * reference, which allocates its activation scratch on every call,
  * kernel/quantized_matmul.cpp:532-534).  For callers that cannot allocate

@@ -73,6 +73,7 @@ class Oracle:
         lib.ql_oracle_rescale.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp]
         lib.ql_oracle_matmul.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp]
         lib.ql_oracle_matmul_i8.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp]
+        lib.ql_oracle_rmsnorm.argtypes = [_vp, _vp, _i, _i, ctypes.c_float, _vp]
         self.lib = lib
 
     def quantize_i16(self, a):
@@ -120,6 +121,16 @@ class Oracle:
         return c
 
 
+    def rmsnorm(self, x, w, eps):
+        """hn = rmsnorm(x) as the reference decoder computes it
+        (``kernel/qwen35_decoder.cpp:133-141``)."""
+        x = np.ascontiguousarray(x, np.float32)
+        M, K = x.shape
+        out = np.empty((M, K), np.float32)
+        self.lib.ql_oracle_rmsnorm(_p(x), _p(np.ascontiguousarray(w, np.float32)), M, K, float(eps), _p(out))
+        return out
+
+
 class Reference:
     """ctypes view of the compiled reference (``_ref/libbreeze_ref.so``)."""
 
@@ -137,6 +148,7 @@ class Reference:
         lib.refprobe_block_sums.restype = _i
         lib.refprobe_replay.argtypes = [_vp, _vp, _vp, _i, _vp]
         lib.refprobe_replay.restype = _i
+        lib.refprobe_rmsnorm.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_float]
         self.lib = lib
         lib.i4_set_numa_split(1 << 30)
 
@@ -185,6 +197,15 @@ class Reference:
         cs = np.empty((M, N, K // 32), np.int32)
         assert self.lib.refprobe_block_sums(_vp(handle), _p(hi), _p(lo), M, _p(cs)) == 0
         return cs
+
+    def rmsnorm(self, x, w, eps):
+        """The reference decoder's own rmsnorm (``kernel/qwen35_decoder.cpp:133-141``),
+        compiled from its source file by ``oracle/ref_norm_probe.cpp``."""
+        x = np.ascontiguousarray(x, np.float32)
+        M, K = x.shape
+        out = np.empty((M, K), np.float32)
+        self.lib.refprobe_rmsnorm(_p(out), _p(x), _p(np.ascontiguousarray(w, np.float32)), M, K, float(eps))
+        return out
 
     def replay(self, handle, cs, ascale, N):
         M = cs.shape[0]

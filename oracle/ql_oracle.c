@@ -30,6 +30,9 @@
  *   - INT8 single-pass mode     kernel/quantized_matmul.cpp:215-232,266-267
  *       (secondary; hi_prec = 0): q = clamp(lrint(a*inv), +-127),
  *       scale = amax / 127.f, cs = sum q8 * (w - zp).
+ *   - RMSNorm prologue          kernel/qwen35_decoder.cpp:133-141
+ *       ss = serial double sum of (double)x*x in j order,
+ *       inv = 1.f / sqrtf((float)(ss / K) + eps), o = (x * inv) * w.
  *
  * Must be compiled with -ffp-contract=off and without -ffast-math so every
  * float operation rounds exactly once, as in the reference.
@@ -196,4 +199,19 @@ void ql_oracle_matmul_i8(const uint8_t* qw, const float* bscale, const uint8_t* 
             }
             C[(size_t)m * N + n] = acc;
         }
+}
+
+/* The reference decoder's rmsnorm (kernel/qwen35_decoder.cpp:133-141): the
+ * sum of squares in double, serially in j order (each (double)x*x is exact,
+ * so contracting it into an fma, as -march builds of the reference may do,
+ * rounds identically), then fp32 for the rest. */
+void ql_oracle_rmsnorm(const float* X, const float* W, int M, int K, float eps, float* out) {
+    for (int m = 0; m < M; ++m) {
+        const float* x = X + (size_t)m * K;
+        float* o = out + (size_t)m * K;
+        double ss = 0.0;
+        for (int j = 0; j < K; ++j) ss += (double)x[j] * (double)x[j];
+        const float inv = 1.0f / sqrtf((float)(ss / K) + eps);
+        for (int j = 0; j < K; ++j) o[j] = (x[j] * inv) * W[j];
+    }
 }

@@ -19,6 +19,10 @@ Input recipes follow the reference's own tests:
     outlier blocks (quantizer corner cases).
   * ``rtn_*``     -- this package's RTN packer on N(0, 0.02) weights with the
     BASELINE distributions (N(0,1) activations, 1% of channels x20), small sizes.
+
+``norm_cases()`` are the RMSNorm prologue's inputs (rows x, weights w, eps);
+``make_golden.py`` stores the reference decoder's own rmsnorm of each
+(``kernel/qwen35_decoder.cpp:133-141``) in ``golden_norm.npz``.
 """
 import hashlib
 
@@ -143,4 +147,59 @@ def input_digest(case):
     for hp, a in case["acts"]:
         h.update(bytes([hp]))
         h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+# ------------------------------------------------------------------ RMSNorm prologue
+def tie_rows(pairs=((3, 38), (4, 45), (5, 30), (6, 37), (7, 2), (10, 3), (2, 1), (1, 2)),
+             exps=(0, -3, 5), K=64):
+    """Rows whose reference mean of squares is decided by the serial order.
+
+    x0 = 1 + a*2^-12 and x1 = b*2^-12 with a^2 + b^2 odd have squares summing
+    exactly to B = 1 + a*2^-11 + (a^2 + b^2)*2^-24, and B / K (K = 64) lies
+    exactly half way between two floats.  The other 62 entries are 2^-28,
+    whose squares (2^-56) each fall below half an ulp of the running double
+    sum and are dropped by the reference's serial loop, so its mean is the tie
+    (rounded to even); any order that adds the small squares first gets a sum
+    above the tie and the next float up.  For the first four pairs that one
+    ulp of the mean also changes 1/sqrt(mean + 0), so hn differs.  Scaling a
+    row by 2^e keeps all of this (squares scale by 4^e).
+    """
+    rows = []
+    for e in exps:
+        for a, b in pairs:
+            r = np.full(K, np.float32(2.0 ** -28), np.float32)
+            r[0] = np.float32(1.0 + a * 2.0 ** -12)
+            r[1] = np.float32(b * 2.0 ** -12)
+            rows.append(r * np.float32(2.0 ** e))
+    return np.stack(rows)
+
+
+def norm_cases():
+    cases = {}
+    rng = np.random.default_rng(21)
+    x = (rng.normal(size=(6, 64)) * rng.uniform(0.01, 30.0, (6, 1))).astype(np.float32)
+    cases["rand_k64"] = (x, rng.uniform(0.5, 2.0, 64).astype(np.float32), 1e-6)
+    # Qwen3.5-27B hidden width, zero-centred norm weights near 1, outlier channels.
+    w = (1.0 + 0.1 * np.random.default_rng(22).normal(size=5120)).astype(np.float32)
+    cases["qwen_k5120"] = (outlier_activations(5, 5120, 23), w, 1e-6)
+    cases["ties"] = (tie_rows(), np.ones(64, np.float32), 0.0)
+    e = np.random.default_rng(24).normal(size=(6, 96)).astype(np.float32)
+    e[0] = 0.0                                   # zero row: inv = 1/sqrt(eps)
+    e[1, 7] = np.nan                             # NaN row
+    e[2, 3] = np.inf                             # inf row: inv = 0
+    e[3] = np.float32(1e-40)                     # subnormal row
+    e[4] = np.float32(3e38)                      # huge row (squares ~1e77 in double)
+    e[5, ::2] = -e[5, ::2]
+    cases["edge_k96"] = (e, np.random.default_rng(25).uniform(-2, 2, 96).astype(np.float32), 1e-6)
+    z = np.zeros((2, 32), np.float32)
+    z[1, 0] = 1.0
+    cases["zero_eps0_k32"] = (z, np.ones(32, np.float32), 0.0)   # 0 * inf = NaN in row 0
+    return cases
+
+
+def norm_digest(x, w, eps):
+    h = hashlib.sha256()
+    for v in (x, w, np.float32(eps)):
+        h.update(np.ascontiguousarray(v).tobytes())
     return h.hexdigest()

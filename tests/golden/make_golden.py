@@ -11,8 +11,13 @@ on every case of ``cases.py``, and stores:
                                sets with a small M*N*nblk only)
   ``<case>/hi<i>``, ``lo<i>``, ``as<i>``  reference quantizer planes (same subset)
 
+It also runs the reference decoder's own ``rmsnorm``
+(``kernel/qwen35_decoder.cpp:133-141``, exported by ``oracle/ref_norm_probe.cpp``)
+on ``cases.norm_cases()`` and stores ``<case>/digest`` and ``<case>/hn`` in
+``golden_norm.npz``.
+
 Run from the repository root where the reference checkout exists:
-``python tests/golden/make_golden.py``.
+``python tests/golden/make_golden.py [--norm-only]``.
 """
 import os
 import sys
@@ -23,15 +28,29 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
-from cases import all_cases, input_digest  # noqa: E402
+from cases import all_cases, input_digest, norm_cases, norm_digest  # noqa: E402
 from oracle.oracle import Reference, build  # noqa: E402
 
 CS_LIMIT = 10_000    # store INT32 accumulators when M*N*nblk is at most this
 
 
+def make_norm(ref):
+    out = {}
+    for name, (x, w, eps) in norm_cases().items():
+        out[f"{name}/digest"] = np.frombuffer(bytes.fromhex(norm_digest(x, w, eps)), np.uint8)
+        out[f"{name}/hn"] = ref.rmsnorm(x, w, eps)
+        print(f"norm {name}: {x.shape}")
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_norm.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+
+
 def main():
     build()
     ref = Reference()
+    make_norm(ref)
+    if "--norm-only" in sys.argv[1:]:
+        return
     out = {}
     for name, make in all_cases().items():
         case = make()

@@ -96,3 +96,56 @@ def quantize_dev(a):
 
 def device_error(clear=True):
     return lib().ql_device_error(1 if clear else 0)
+
+
+def rmsnorm_quantize_dev(x, w, eps, hi_prec, want_hn=True):
+    """ql_quantize_act_rmsnorm_dev: returns (workspace tensor, hn or None)."""
+    import torch
+    x = np.ascontiguousarray(x, np.float32)
+    M, K = x.shape
+    dX = torch.from_numpy(x).cuda()
+    dW = torch.from_numpy(np.ascontiguousarray(w, np.float32)).cuda()
+    need = lib().ql_norm_act_workspace_bytes(M, K)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    hn = torch.full((M, K), -7.0, dtype=torch.float32, device="cuda") if want_hn else None
+    rc = lib().ql_quantize_act_rmsnorm_dev(dX.data_ptr(), dW.data_ptr(), float(eps), M, K, 1 if hi_prec else 0,
+                                           ws.data_ptr(), need, hn.data_ptr() if want_hn else None,
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return ws, (hn.cpu().numpy() if want_hn else None)
+
+
+def matmul_quantized_dev(h, ws, M, hi_prec, N):
+    """ql_matmul_quantized_dev over a workspace filled by a quantize call."""
+    import torch
+    dC = torch.full((M, N), -12345.0, dtype=torch.float32, device="cuda")
+    rc = lib().ql_matmul_quantized_dev(_vp(h), ws.data_ptr(), M, 1 if hi_prec else 0, dC.data_ptr(),
+                                       torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return dC.cpu().numpy()
+
+
+def matmul_rmsnorm_dev(h, x, w, eps, N):
+    """ql_matmul_rmsnorm_dev (library workspace, process-wide activation mode)."""
+    import torch
+    x = np.ascontiguousarray(x, np.float32)
+    M = x.shape[0]
+    dX = torch.from_numpy(x).cuda()
+    dW = torch.from_numpy(np.ascontiguousarray(w, np.float32)).cuda()
+    dC = torch.full((M, N), -12345.0, dtype=torch.float32, device="cuda")
+    rc = lib().ql_matmul_rmsnorm_dev(_vp(h), dX.data_ptr(), dW.data_ptr(), float(eps), M, dC.data_ptr(),
+                                     torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return dC.cpu().numpy()
+
+
+def concat(handles):
+    """ql_weight_concat: one handle stacking the weights along N."""
+    arr = (_vp * len(handles))(*handles)
+    out = _vp()
+    rc = lib().ql_weight_concat(arr, len(handles), ctypes.byref(out))
+    assert rc == 0 and out.value, lib().ql_error_string(rc)
+    return out.value
