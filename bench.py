@@ -16,6 +16,14 @@ Workloads (``--workload``):
   two-pass INT16.  One step is the 3 calls.  ``value`` is INT8 tera-operations
   per second counted as BASELINE.md does: ``4*M*N*K`` per call (two INT8
   passes of 2*M*N*K each).
+* ``mlp_front``: the front of a Qwen3.5-27B MLP block at decode batch sizes
+  (M in {1, 4, 8, 16}; H = 5120, intermediate 17408, INT4 with fp16 scales):
+  the RMSNorm fused into the activation quantizer, then one decode launch over
+  the concatenated [gate; up] weight.  ``value`` is HBM GB/s of the step's
+  algorithmic bytes; ``parts`` times the same step with gate and up as two
+  launches and with the norm left out.  The reference arm runs the
+  reference's own rmsnorm and two i4_matmul per M.  ``--gpus P`` runs P
+  replicas.
 
 With ``--gpus P`` every layer is column-parallel (N/P per GPU) and the output
 shards are NCCL-all-gathered: total work is fixed, so scaling is "strong".
@@ -492,7 +500,229 @@ class ShardedWorkload(_OpsOrBytes):
         return f"the two layers at M={min(self.M, 128)}"
 
 
-WORKLOADS = {"decode": DecodeWorkload, "prefill": PrefillWorkload,
+class MlpFrontWorkload:
+    """The front of a Qwen3.5-27B MLP block at decode batch sizes: the
+    reference decoder's rmsnorm, then gate and up on the normalised rows
+    (kernel/qwen35_decoder.cpp:405-407; H = 5120, intermediate 17408, INT4
+    weights with fp16 scales).  Here: ql_quantize_act_rmsnorm_dev (row factors
+    + quantizer with the norm fused in) and ONE decode launch over the
+    concatenated [gate; up] weight (ql_weight_concat).  Every rank runs the
+    same independent work (replicas)."""
+    name = "mlp_front"
+    metric = "fused RMSNorm + gate|up decode HBM throughput (INT4 weights, two-pass INT16 activations)"
+    unit = "GB/s"
+    H, INTER = 5120, 17408
+    Ms = [1, 4, 8, 16]
+    bits = 4
+    eps = 1e-6
+    copies = 3                    # 3 x 100 MB of [gate; up] rotated: each call streams from HBM
+    kernel = "decode_kernel (ql_gemv.cu) on the concatenated gate|up weight"
+    cpu_sample = "full sweeps (per M: the reference rmsnorm + gate and up i4_matmul)"
+
+    def step_amount(self):
+        """Algorithmic bytes of one step: per M the gate|up weights and fp16
+        scales, the rows x, the norm weights and the outputs."""
+        return sum(alg_bytes(M, self.H, 2 * self.INTER, self.bits) + 4 * self.H for M in self.Ms)
+
+    def value(self, amount, seconds):
+        return amount / seconds / 1e9
+
+    def config(self, world):
+        return {"workload": "MLP front of Qwen3.5-27B (rmsnorm -> gate, up) at decode batch sizes",
+                "M": self.Ms, "H": self.H, "intermediate": self.INTER,
+                "weights": "INT4 symmetric RTN, fp16 scales (gate and up concatenated along N)",
+                "activations": "two-pass INT16 (hi_prec=1); rows N(0,1), 1% channels x20",
+                "l2": f"{self.copies} rotated weight copies (300 MB); each call streams from HBM",
+                "timing": "CUDA graph of one step (per M: norm factors, fused quantize, one matmul), CUDA events",
+                "parallelism": "1 GPU" if world == 1 else f"replicas on {world} GPUs (no collective)"}
+
+
+def run_mlp_front(args):
+    import torch
+    import torch.distributed as dist
+    from breeze_engine_b200 import _lib as L
+    from breeze_engine_b200 import backend
+
+    wl = MlpFrontWorkload()
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = L.load()
+    backend.set_hi_prec(True)
+    H, I = wl.H, wl.INTER
+    gate = Layer(lib, H, I, wl.bits, 1, 0, 2001, wl.copies)
+    up = Layer(lib, H, I, wl.bits, 1, 0, 2002, wl.copies)
+    both = [backend.concat_packed([g, u]) for g, u in zip(gate.handles, up.handles)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2003)
+    norm_w = (1.0 + 0.1 * torch.randn(H, generator=g, device="cuda")).float()
+    xs = {M: _outlier_acts(M, H, 2100 + M) for M in wl.Ms}
+    nws = {M: lib.ql_norm_act_workspace_bytes(M, H) for M in wl.Ms}
+    wss = {M: torch.empty(nws[M], dtype=torch.uint8, device="cuda") for M in wl.Ms}
+    outs = {M: torch.empty((M, 2 * I), dtype=torch.float32, device="cuda") for M in wl.Ms}
+    outs_g = {M: torch.empty((M, I), dtype=torch.float32, device="cuda") for M in wl.Ms}
+    outs_u = {M: torch.empty((M, I), dtype=torch.float32, device="cuda") for M in wl.Ms}
+    stream = torch.cuda.current_stream()
+
+    def ok(rc, what):
+        if rc:
+            raise RuntimeError(f"{what} failed: {lib.ql_error_string(rc)}")
+
+    def quant_norm(M, s):
+        ok(lib.ql_quantize_act_rmsnorm_dev(xs[M].data_ptr(), norm_w.data_ptr(), wl.eps, M, H, 1,
+                                           wss[M].data_ptr(), nws[M], None, s), "quantize+norm")
+
+    def fused(j, M, s):
+        quant_norm(M, s)
+        ok(lib.ql_matmul_quantized_dev(ctypes.c_void_p(both[j % wl.copies]), wss[M].data_ptr(), M, 1,
+                                       outs[M].data_ptr(), s), "matmul")
+
+    def separate(j, M, s):
+        quant_norm(M, s)
+        for hs, o in ((gate.handles, outs_g), (up.handles, outs_u)):
+            ok(lib.ql_matmul_quantized_dev(ctypes.c_void_p(hs[j % wl.copies]), wss[M].data_ptr(), M, 1,
+                                           o[M].data_ptr(), s), "matmul")
+
+    def no_norm(j, M, s):
+        ok(lib.ql_quantize_act_dev(xs[M].data_ptr(), M, H, 1, wss[M].data_ptr(), nws[M], s), "quantize")
+        ok(lib.ql_matmul_quantized_dev(ctypes.c_void_p(both[j % wl.copies]), wss[M].data_ptr(), M, 1,
+                                       outs[M].data_ptr(), s), "matmul")
+
+    def matmul_only(j, M, s):
+        ok(lib.ql_matmul_quantized_dev(ctypes.c_void_p(both[j % wl.copies]), wss[M].data_ptr(), M, 1,
+                                       outs[M].data_ptr(), s), "matmul")
+
+    def make_graph(body):
+        for _ in range(2):
+            for j, M in enumerate(wl.Ms):
+                body(j, M, stream.cuda_stream)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            s = torch.cuda.current_stream().cuda_stream
+            for j, M in enumerate(wl.Ms):
+                body(j, M, s)
+        return gr
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(t):
+        if world > 1:
+            tt = torch.tensor([t], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    def timed(gr, n):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / 1e3)
+
+    graphs = {name: make_graph(body) for name, body in
+              (("fused", fused), ("separate", separate), ("no_norm", no_norm))}
+    # self-check: one launch over [gate; up] == the two separate launches, bit for bit
+    graphs["fused"].replay()
+    graphs["separate"].replay()
+    torch.cuda.synchronize()
+    for M in wl.Ms:
+        if not (torch.equal(outs[M][:, :I].view(torch.int32), outs_g[M].view(torch.int32)) and
+                torch.equal(outs[M][:, I:].view(torch.int32), outs_u[M].view(torch.int32))):
+            raise RuntimeError(f"concatenated gate|up differs from separate launches at M={M}")
+
+    for _ in range(args.warmup):
+        graphs["fused"].replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t_probe = timed(graphs["fused"], 3) / 3
+    timed(graphs["fused"], max(1, int(1.0 / max(t_probe, 1e-6))))
+    t = timed(graphs["fused"], args.steps)
+    clock_info = clocks.stop()
+    clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
+    parts = {"fused_us_per_step": round(t / args.steps * 1e6, 2)}
+    for name in ("separate", "no_norm"):
+        for _ in range(args.warmup):
+            graphs[name].replay()
+        parts[f"{name}_us_per_step"] = round(timed(graphs[name], args.steps) / args.steps * 1e6, 2)
+    amount = wl.step_amount()
+    value = world * wl.value(amount * args.steps, t)
+
+    # the matmul kernel alone (its activations quantized above), for the roofline
+    gk = make_graph(matmul_only)
+    for _ in range(args.warmup):
+        gk.replay()
+    tk = timed(gk, args.steps) / args.steps
+    kern_amount = sum(decode_kernel_bytes(M, H, 2 * I, wl.bits) for M in wl.Ms)
+    achieved = kern_amount / tk / 1e9
+    peak, kind = measured_peaks()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "kernel": wl.kernel, "us_per_launch": round(tk / len(wl.Ms) * 1e6, 2)}
+
+    # end to end: x from pinned host memory, the fused calls, outputs back to pinned memory
+    e2e = None
+    if not args.no_e2e:
+        hx = {M: xs[M].cpu().pin_memory() for M in wl.Ms}
+        hc = {M: torch.empty((M, 2 * I), dtype=torch.float32).pin_memory() for M in wl.Ms}
+
+        def e2e_step():
+            for j, M in enumerate(wl.Ms):
+                xs[M].copy_(hx[M], non_blocking=True)
+                fused(j, M, stream.cuda_stream)
+                hc[M].copy_(outs[M], non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        t_e2e = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": round(world * wl.value(amount * args.steps, t_e2e), 2), "unit": wl.unit,
+               "h2d_bytes_per_step": int(sum(4 * M * H for M in wl.Ms)),
+               "d2h_bytes_per_step": int(sum(4 * M * 2 * I for M in wl.Ms)),
+               "api": "ql_quantize_act_rmsnorm_dev + ql_matmul_quantized_dev, pinned host buffers"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = mlp_front_cpu(wl, samples=2)
+    if rank == 0:
+        line = {"metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "s8xs8/u8->s32, f32 rescale; f64 row sums",
+                "data": "synthetic (seeded N(0,0.02) weights, N(0,1) rows with outlier channels)",
+                "config": wl.config(world), "roofline": roofline, "parts": parts,
+                "gpu_launches": 3 * len(wl.Ms) * args.steps, "clocks": clock_info}
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    del graphs, gk
+    for h in both:
+        backend.free(h)
+    gate.free()
+    up.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+WORKLOADS = {"decode": DecodeWorkload, "prefill": PrefillWorkload, "mlp_front": MlpFrontWorkload,
              "layer_m1": lambda: LayerSetWorkload(1), "layer_m512": lambda: LayerSetWorkload(512),
              "sharded_m1": lambda: ShardedWorkload(1), "sharded_m2048": lambda: ShardedWorkload(2048)}
 
@@ -794,6 +1024,65 @@ def cpu_baseline(wl, samples=2):
                       f"OpenMP {threads} threads, OMP_PROC_BIND=spread"}
 
 
+class _RefMlpFront:
+    """The reference decoder's MLP front on the host: its own rmsnorm
+    (kernel/qwen35_decoder.cpp:133-141, through oracle/ref_norm_probe.cpp) and
+    i4_matmul for gate and up (:406-407), per M of the workload."""
+
+    def __init__(self, ref, wl, threads):
+        self.ref, self.wl = ref, wl
+        H, I = wl.H, wl.INTER
+        self.handles = []
+        for i in range(2):
+            qw, sc = host_weights(H, I, wl.bits, 300 + i)
+            self.handles.append(ref.prepack(qw, sc, None, H, I, wl.bits))
+            del qw
+        rng = np.random.default_rng(9)
+        self.norm_w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        self.xs = {M: rng.standard_normal((M, H)).astype(np.float32) for M in wl.Ms}
+        self.hn = {M: np.empty((M, H), np.float32) for M in wl.Ms}
+        self.outs = {M: np.empty((M, I), np.float32) for M in wl.Ms}
+        ref.lib.i4_set_threads(threads)
+        ref.lib.i4_set_hi_prec(1)
+
+    def step(self):
+        lib = self.ref.lib
+        for M in self.wl.Ms:
+            lib.refprobe_rmsnorm(self.hn[M].ctypes.data, self.xs[M].ctypes.data, self.norm_w.ctypes.data,
+                                 M, self.wl.H, ctypes.c_float(self.wl.eps))
+            for h in self.handles:
+                lib.i4_matmul(ctypes.c_void_p(h), self.hn[M].ctypes.data, M, self.outs[M].ctypes.data)
+
+    def amount(self, wl):
+        return wl.step_amount()
+
+    def free(self):
+        for h in self.handles:
+            self.ref.free(h)
+
+
+def mlp_front_cpu(wl, samples=2):
+    """cpu_baseline of the MLP-front workload (the reference's rmsnorm + two
+    i4_matmul per M, OpenMP on all host threads)."""
+    os.environ.setdefault("OMP_PROC_BIND", "spread")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref, why = _reference_lib()
+    if ref is None:
+        return {"value": None, "unit": wl.unit, "cores": 0, "kind": "reference", "sample": why}
+    threads = os.cpu_count() or 1
+    rc = _RefMlpFront(ref, wl, threads)
+    rc.step()
+    t0 = time.perf_counter()
+    for _ in range(samples):
+        rc.step()
+    dt = time.perf_counter() - t0
+    rc.free()
+    return {"value": round(wl.value(wl.step_amount() * samples, dt), 2), "unit": wl.unit, "cores": threads,
+            "kind": "reference", "ms_per_step": round(dt / samples * 1e3, 2),
+            "sample": f"{samples} x {wl.cpu_sample} after 1 warm-up, set_hi_prec(1), "
+                      f"OpenMP {threads} threads, OMP_PROC_BIND=spread"}
+
+
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -806,9 +1095,12 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
     threads = os.cpu_count() or 1
-    spec = ([(wl.K, wl.N, wl.bits, wl.Ms)] if wl.name == "prefill" else
-            [(K, N, b, [wl.M]) for K, N, b, _ in wl.cpu_calls()] if hasattr(wl, "M") else wl.cpu_calls())
-    rc = _RefCalls(ref, spec, threads)
+    if wl.name == "mlp_front":
+        rc = _RefMlpFront(ref, wl, threads)
+    else:
+        spec = ([(wl.K, wl.N, wl.bits, wl.Ms)] if wl.name == "prefill" else
+                [(K, N, b, [wl.M]) for K, N, b, _ in wl.cpu_calls()] if hasattr(wl, "M") else wl.cpu_calls())
+        rc = _RefCalls(ref, spec, threads)
     for _ in range(args.warmup):
         rc.step()
     t0 = time.perf_counter()
@@ -824,7 +1116,8 @@ def run_reference(args):
     line = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "u8xs8->s32 (VPDPBUSD), f32 rescale",
+            "scaling": "weak" if wl.name == "mlp_front" else "strong", "vs_baseline": None,
+            "dtype": "u8xs8->s32 (VPDPBUSD), f32 rescale",
             "data": "synthetic (random MatMulNBits codes, fp16 scales; N(0,1) activations)",
             "config": cfg,
             "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "reference",
@@ -879,6 +1172,8 @@ def main(argv=None):
         run_ncu_case(*map(int, args.ncu_case.split(",")))
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mlp_front":
+        run_mlp_front(args)
     else:
         run_ours(args)
     return 0

@@ -47,3 +47,15 @@ def test_sharded_shapes_divide(world):
     for K, N in col:
         assert N % (16 * world) == 0, (K, N, world)
     assert (65536 // 32) % world == 0
+
+
+def test_mlp_front_workload_streams_from_hbm():
+    """The fused MLP-front bench: decode-size batches (one decode launch per
+    call), a concatenated width in whole 16-row groups, and rotated weight
+    copies whose total is well above the 126 MB L2 so each call reads HBM."""
+    wl = bench.MlpFrontWorkload
+    assert max(wl.Ms) <= 64
+    assert (2 * wl.INTER) % 16 == 0 and wl.H % 32 == 0
+    one = bench.alg_bytes(0, wl.H, 2 * wl.INTER, wl.bits)
+    assert wl.copies * one > 2 * bench.L2_BYTES
+    assert wl().step_amount() == sum(bench.alg_bytes(M, wl.H, 2 * wl.INTER, wl.bits) + 4 * wl.H for M in wl.Ms)
