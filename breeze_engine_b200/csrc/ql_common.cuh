@@ -69,6 +69,17 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy ones.  Every thread that read a stage filled by a bulk copy runs
+// it before the stage is handed back to the producer: the mbarrier release
+// alone does not order those reads against the next bulk copy's writes into
+// the same bytes (measured on B200: without it the decode kernel, releasing
+// each stage before its relay wait, intermittently produced wrong outputs for
+// its last token groups at 57-64 tokens; with it, none in repeated runs).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile("{\n\t.reg .pred p;\n\t"

@@ -389,6 +389,7 @@ __global__ void __launch_bounds__(NWARPS * 32, 1) gemm_kernel(const GemmParams p
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&acc_empty[ac]));
                 }
+                fence_proxy_async_smem();      // scale reads of this stage before its refill
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(smem_u32(&stage_empty[s]));
             }

@@ -259,6 +259,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
             // producer before the (serial) relay wait and FFMA chain, so the
             // ring refills while the chain runs.
             if (j0 + C >= nb) {
+                fence_proxy_async_smem();      // this warp's reads before the refill's bulk copy
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
             }
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
         }
         // release the stage to the producer (the FP32 path released it above)
         if (OUT_CS) {
+            fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
             continue;

@@ -68,9 +68,9 @@ def test_fused_matmul_equals_matmul_of_reference_rows(M, bits, zp, half, hp, ora
     try:
         qlc.set_hi_prec(hp)
         fused = qlc.matmul_rmsnorm_dev(h, x, w, 1e-6, N)
-        assert bits_equal(fused, qlc.matmul_dev(h, hn, N))
-        if M <= 3:
-            assert bits_equal(fused, oracle.matmul(qw, sc, qz, N, K, bits, hn, hi_prec=hp))
+        want = oracle.matmul(qw, sc, qz, N, K, bits, hn, hi_prec=hp)
+        assert bits_equal(fused, want)
+        assert bits_equal(qlc.matmul_dev(h, hn, N), want)
     finally:
         qlc.free(h)
 

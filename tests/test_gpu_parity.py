@@ -4,6 +4,8 @@ Every call goes through the C ABI (tests/qlc.py).  The bar is bit-exact: the
 activation planes and scales, the per-block INT32 accumulators, and the FP32
 outputs (the kernels run each output's rescale chain in reference block order).
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -267,4 +269,38 @@ def test_host_call_output_chunks(M, N, K, bits):
         assert bits_equal(qlc.matmul_host(h, a, N), qlc.matmul_dev(h, a, N))
     finally:
         qlc.set_hi_prec(False)
+        qlc.free(h)
+
+
+@pytest.mark.parametrize("bits,half,N,K,M,cfg", [
+    (8, False, 96, 5120, 64, None), (8, False, 96, 5120, 57, None), (8, True, 96, 5120, 64, None),
+    (8, False, 32, 2048, 64, None), (8, False, 96, 5120, 64, "1,4,2,4"), (8, False, 96, 5120, 64, "2,4,2,8"),
+    (4, True, 96, 5120, 64, "1,4,2,8"), (4, True, 96, 5120, 64, "1,8,2,8")])
+def test_split_k_relay_repeatable(bits, half, N, K, M, cfg, oracle, monkeypatch):
+    """K split across warps with one sub-chunk per stage (each warp hands its
+    stage back before it waits for the relay): the last token groups must be
+    right on every run.  These shapes and tuning overrides once failed
+    intermittently (rows 48-63), until every stage release was preceded by an
+    async-proxy fence."""
+    import torch
+    if cfg:
+        monkeypatch.setenv("BREEZE_QL_DECODE_CONFIG", cfg)
+    qw, sc, qz = fixture_weights(N, K, bits, np.float16 if half else np.float32, False)
+    a = outlier_activations(M, K, 43 + M)
+    ref = oracle.matmul(qw, sc, qz, N, K, bits, a)
+    h = qlc.prepack(qw, sc, qz, N, K, bits)
+    lib = qlc.lib()
+    try:
+        qlc.set_hi_prec(True)
+        dA = torch.from_numpy(a).cuda()
+        n = lib.ql_act_workspace_bytes(M, K)
+        ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        assert lib.ql_quantize_act_dev(dA.data_ptr(), M, K, 1, ws.data_ptr(), n, s) == 0
+        for _ in range(10):
+            c = torch.full((M, N), -1.0, device="cuda")
+            assert lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s) == 0
+            torch.cuda.synchronize()
+            assert bits_equal(c.cpu().numpy(), ref)
+    finally:
         qlc.free(h)
