@@ -649,18 +649,19 @@ size_t norm_ws_bytes(int M, int nblk) {
 int run_quantize_norm(const float* dX, const float* dW, float eps, int M, int K, void* ws, float* dHn,
                       cudaStream_t stream, bool hi_prec) {
     const int nblk = K / 32;
-    float* row_inv = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256(ws_bytes_for(M, nblk)));
-    cudaError_t e = launch_rmsnorm_factors(dX, K, M, K, eps, row_inv, stream);
-    if (e != cudaSuccess) return cuda_status(e);
     if (use_gemm(M)) {
+        // row factors into the workspace's tail, then the GEMM-layout quantizer
+        float* row_inv = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + align256(ws_bytes_for(M, nblk)));
+        cudaError_t e = launch_rmsnorm_factors(dX, K, M, K, eps, row_inv, stream);
+        if (e != cudaSuccess) return cuda_status(e);
         const NormArgs n{row_inv, dW, dHn, K};
         return cuda_status(launch_quantize_gemm(dX, K, M, K, hi_prec, static_cast<uint8_t*>(ws), stream, &n));
     }
-    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
+    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {    // factors and quantizer in one launch per chunk
         const ActView act = chunk_view(ws, M, nblk, c, hi_prec);
         const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
-        const NormArgs n{row_inv + m0, dW, dHn ? dHn + m0 * K : nullptr, K};
-        e = launch_quantize_act(dX + m0 * K, K, act.M, K, hi_prec, act, stream, &n);
+        const NormArgs n{nullptr, dW, dHn ? dHn + m0 * K : nullptr, K};
+        cudaError_t e = launch_quantize_act_norm(dX + m0 * K, K, act.M, K, eps, hi_prec, act, n, stream);
         if (e != cudaSuccess) return cuda_status(e);
     }
     return set_status(QL_OK);

@@ -84,6 +84,10 @@ struct NormArgs {
 // row_inv[m] for M rows of X (ldx floats apart, K wide), ql_norm.cu.
 cudaError_t launch_rmsnorm_factors(const float* X, int ldx, int M, int K, float eps, float* row_inv,
                                    cudaStream_t stream);
+// Decode layout (M <= 64): the row factors and the quantizer with the norm
+// applied in one launch (one CTA per token row), ql_norm.cu.
+cudaError_t launch_quantize_act_norm(const float* X, int ldx, int M, int K, float eps, bool hi_prec,
+                                     const ActView& out, const NormArgs& nrm, cudaStream_t stream);
 
 constexpr int MAX_DECODE_TOKENS = 64;                    // MT <= 8 token groups
 

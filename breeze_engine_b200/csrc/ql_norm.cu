@@ -5,8 +5,10 @@
 //   double ss = 0; for j: ss += (double)x[j] * x[j];      // serial, in j order
 //   float inv = 1.0f / std::sqrt((float)(ss / H) + eps);
 //   o[j] = x[j] * inv * w[j];
-// This file computes inv per row bit-exactly; the quantizers apply the last
-// line (ql_quant.cu, load_block).
+// This file computes inv per row bit-exactly.  For the tensor-core GEMM layout
+// (more than 64 tokens) rmsnorm_factor_kernel writes the factors and the GEMM
+// quantizer applies the last line (ql_quant.cuh, load_block); for the decode
+// layout quantize_act_norm_kernel does both in one launch, one CTA per row.
 //
 // Every square (double)x*x of a finite float is exact in double (24-bit
 // significands give 48-bit products, and the exponent range of a float
@@ -27,6 +29,7 @@
 
 #include "ql_common.cuh"
 #include "ql_internal.h"
+#include "ql_quant.cuh"
 
 namespace ql {
 
@@ -56,16 +59,9 @@ __device__ float certified_mean(const float* __restrict__ x, int K, double p) {
 
 constexpr int NORM_THREADS = 256;
 
-__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_factor_kernel(const float* __restrict__ X, int ldx,
-                                                                      int M, int K, float eps,
-                                                                      float* __restrict__ row_inv) {
-    // Launched with PDL: the producer of X may still be draining.  The
-    // quantizer that reads row_inv waits for this whole grid.
-    pdl_launch_dependents();
-    pdl_wait();
-    const int m = blockIdx.x;
-    if (m >= M) return;
-    const float* x = X + static_cast<size_t>(m) * ldx;
+// inv = 1/sqrt(mean(x^2) + eps) of one row, computed by the whole CTA
+// (NORM_THREADS threads, all of which must call it); every thread gets it.
+__device__ float block_row_inv(const float* __restrict__ x, int K, float eps) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     double s = 0.0;
     for (int i = threadIdx.x; i < K / 4; i += NORM_THREADS) {
@@ -76,6 +72,7 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_factor_kernel(const floa
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     __shared__ double part[NORM_THREADS / 32];
+    __shared__ float inv;
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -83,8 +80,63 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_factor_kernel(const floa
 #pragma unroll
         for (int w = 0; w < NORM_THREADS / 32; ++w) p += part[w];
         const float mean = certified_mean(x, K, p);
-        row_inv[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     }
+    __syncthreads();
+    return inv;
+}
+
+// Row factors for the GEMM-layout quantizer (M > 64 tokens), one CTA per row.
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_factor_kernel(const float* __restrict__ X, int ldx,
+                                                                      int M, int K, float eps,
+                                                                      float* __restrict__ row_inv) {
+    // Launched with PDL: the producer of X may still be draining.  The
+    // quantizer that reads row_inv waits for this whole grid.
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.x;
+    if (m >= M) return;
+    const float r = block_row_inv(X + static_cast<size_t>(m) * ldx, K, eps);
+    if (threadIdx.x == 0) row_inv[m] = r;
+}
+
+// Decode layout (up to 64 tokens): one CTA per token row computes the row's
+// factor and then quantizes the row's blocks with the norm applied, in one
+// launch; CTAs of padded rows (M..TPBA-1) write their zero records.
+template <bool HP>
+__global__ void __launch_bounds__(NORM_THREADS) quantize_act_norm_kernel(const float* __restrict__ X, int ldx,
+                                                                         int M, int K, float eps, ActView out,
+                                                                         NormArgs nrm) {
+    pdl_launch_dependents();   // the matmul may start streaming its weights
+    pdl_wait();
+    const int m = blockIdx.x;
+    const int nblk = K / BLOCK_K;
+    if (m >= M) {
+        for (int b = threadIdx.x; b < nblk; b += NORM_THREADS) act_zero_block<HP>(out, m, b);
+        return;
+    }
+    const float r = block_row_inv(X + static_cast<size_t>(m) * ldx, K, eps);
+    for (int b = threadIdx.x; b < nblk; b += NORM_THREADS) {
+        float v[32];
+        load_raw_block(X, ldx, m, b, v);
+        norm_block(v, r, nrm, m, b);
+        act_store_block<HP>(v, out, m, b);
+    }
+}
+
+cudaError_t launch_norm(void (*kern)(const float*, int, int, int, float, ActView, NormArgs), unsigned grid,
+                        cudaStream_t stream, const float* X, int ldx, int M, int K, float eps, const ActView& out,
+                        const NormArgs& nrm) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NORM_THREADS);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, X, ldx, M, K, eps, out, nrm);
 }
 
 }  // namespace
@@ -102,6 +154,14 @@ cudaError_t launch_rmsnorm_factors(const float* X, int ldx, int M, int K, float 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, rmsnorm_factor_kernel, X, ldx, M, K, eps, row_inv);
+}
+
+cudaError_t launch_quantize_act_norm(const float* X, int ldx, int M, int K, float eps, bool hi_prec,
+                                     const ActView& out, const NormArgs& nrm, cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>(out.TPBA);
+    if (hi_prec) return launch_norm(quantize_act_norm_kernel<true>, grid, stream, X, ldx, M, K, eps, out, nrm);
+    return launch_norm(quantize_act_norm_kernel<false>, grid, stream, X, ldx, M, K, eps, out, nrm);
 }
 
 }  // namespace ql

@@ -15,48 +15,9 @@
 // and writes 16-byte chunks of each plane, so the kernel is a single HBM pass.
 #include "ql_common.cuh"
 #include "ql_internal.h"
+#include "ql_quant.cuh"
 
 namespace ql {
-
-__device__ __forceinline__ int to_int_like_lrint(float x) {
-    const float ax = fabsf(x);
-    if (ax < 2147483648.0f) return __float2int_rn(x);
-    if (ax < 9.2233720368547758e18f) return static_cast<int>(static_cast<uint32_t>(
-                                                static_cast<unsigned long long>(__float2ll_rn(x))));
-    return 0;   // NaN, +-inf, |x| >= 2^63
-}
-
-// The 32 values of (token m, block b): row m of A itself or, with the RMSNorm
-// prologue (NORM), a = (x * row_inv[m]) * w[k] as the reference decoder's
-// rmsnorm writes them (kernel/qwen35_decoder.cpp:139: x * inv * w, evaluated
-// left to right, each product rounded to fp32), stored to hn when it is set.
-template <bool NORM>
-__device__ __forceinline__ void load_block(const float* __restrict__ A, int lda, int m, int b,
-                                           const NormArgs& nrm, float (&v)[32]) {
-    const float4* src = reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 f = __ldg(src + i);
-        v[4 * i + 0] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
-    if (NORM) {
-        const float r = __ldg(nrm.row_inv + m);
-        const float4* w4 = reinterpret_cast<const float4*>(nrm.w + b * BLOCK_K);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 g = __ldg(w4 + i);
-            v[4 * i + 0] = __fmul_rn(__fmul_rn(v[4 * i + 0], r), g.x);
-            v[4 * i + 1] = __fmul_rn(__fmul_rn(v[4 * i + 1], r), g.y);
-            v[4 * i + 2] = __fmul_rn(__fmul_rn(v[4 * i + 2], r), g.z);
-            v[4 * i + 3] = __fmul_rn(__fmul_rn(v[4 * i + 3], r), g.w);
-        }
-        if (nrm.hn) {
-            float4* dst = reinterpret_cast<float4*>(nrm.hn + static_cast<size_t>(m) * nrm.ldh + b * BLOCK_K);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-    }
-}
 
 template <bool HP, bool NORM>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ A, int lda,
@@ -72,65 +33,13 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     if (idx >= static_cast<long long>(out.TPBA) * nblk) return;
     const int m = static_cast<int>(idx / nblk);
     const int b = static_cast<int>(idx % nblk);
-
-    // Block b's record: fragment slots t = 0..3 of token m (lanes 4*(m%8) + t),
-    // then the block's activation scales.
-    constexpr int LB = HP ? 16 : 8;                                   // bytes per lane
-    uint8_t* rec = out.q + static_cast<size_t>(b) * out.QREC;
-    uint8_t* frag = rec + m * 4 * LB;
-    float* scales = reinterpret_cast<float*>(rec + out.TPB * 4 * LB);
-
     if (m >= M) {   // padded token rows
-        if (m < out.TPB) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                if (HP) *reinterpret_cast<uint4*>(frag + t * LB) = make_uint4(0, 0, 0, 0);
-                else *reinterpret_cast<uint2*>(frag + t * LB) = make_uint2(0, 0);
-            }
-        }
-        scales[m] = 0.0f;
+        act_zero_block<HP>(out, m, b);
         return;
     }
-
     float v[32];
     load_block<NORM>(A, lda, m, b, nrm, v);
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const float a = fabsf(v[i]);
-        amax = (a > amax) ? a : amax;
-    }
-    constexpr float QMAX = HP ? 32767.0f : 127.0f;
-    constexpr int IMAX = HP ? 32767 : 127;
-    const float scale = __fdiv_rn(amax, QMAX);
-    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    scales[m] = scale;
-
-    uint32_t hw[8], lw[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-        uint32_t hword = 0, lword = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            int q = to_int_like_lrint(__fmul_rn(v[4 * w + j], inv));
-            q = q > IMAX ? IMAX : (q < -IMAX ? -IMAX : q);
-            if (HP) {
-                const uint32_t u = static_cast<uint32_t>(q + 32768);
-                hword |= ((u >> 8) ^ 0x80u) << (8 * j);      // hi - 128 as a signed byte
-                lword |= (u & 0xFFu) << (8 * j);
-            } else {
-                lword |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);   // q8 as a signed byte
-            }
-        }
-        hw[w] = hword;
-        lw[w] = lword;
-    }
-    // lane t: k 4t..4t+3 (word t) and 16+4t..16+4t+3 (word 4+t) of each plane
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        if (HP) *reinterpret_cast<uint4*>(frag + t * LB) = make_uint4(hw[t], hw[4 + t], lw[t], lw[4 + t]);
-        else *reinterpret_cast<uint2*>(frag + t * LB) = make_uint2(lw[t], lw[4 + t]);
-    }
+    act_store_block<HP>(v, out, m, b);
 }
 
 // GEMM-layout variant (M > 64, ql_gemm16.cu / ql_gemm.cu): the token-half-major
