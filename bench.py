@@ -618,14 +618,16 @@ def run_mlp_front(args):
             t = float(tt.item())
         return t
 
-    def timed(gr, n):
+    def timed(gr, n, label="bench"):
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(label)          # lets ncu --nvtx restrict a capture to it
         e0.record(stream)
         for _ in range(n):
             gr.replay()
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
         return max_over_ranks(e0.elapsed_time(e1) / 1e3)
@@ -648,7 +650,7 @@ def run_mlp_front(args):
     clocks.start()
     t_probe = timed(graphs["fused"], 3) / 3
     timed(graphs["fused"], max(1, int(1.0 / max(t_probe, 1e-6))))
-    t = timed(graphs["fused"], args.steps)
+    t = timed(graphs["fused"], args.steps, label="timed")
     clock_info = clocks.stop()
     clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
     parts = {"fused_us_per_step": round(t / args.steps * 1e6, 2)}
