@@ -750,6 +750,12 @@ def run_ours(args):
 
     layers, acts, calls = wl.build(lib, world, rank)
     owners = getattr(wl, "owners", {})
+    exchange = None
+    if world > 1 and args.exchange == "peer":
+        # one peer-memory exchange sized for the largest column-parallel output
+        from breeze_engine_b200.sharded import PeerExchange
+        cap = max([4 * M * layer.N for layer, _, M in calls if layer.mode == "col"] or [16])
+        exchange = PeerExchange(cap)
 
     def mine(layer, M):
         """Whether this rank runs the call: every rank for sharded layers, the
@@ -782,7 +788,10 @@ def run_ours(args):
                 raise RuntimeError(f"ql_matmul_dev_ws failed: {rc}")
             if world > 1:
                 if layer.mode == "col":
-                    gather_columns(c)
+                    if exchange is not None:
+                        exchange.gather(c)
+                    else:
+                        gather_columns(c)
                 elif layer.mode == "row":
                     reduce_partials(c, "scatter")
 
@@ -919,13 +928,17 @@ def run_ours(args):
         cpu = cpu_baseline(wl, samples=2)
 
     if rank == 0:
+        cfg = wl.config(world)
+        if world > 1 and any(layer.mode == "col" for layer, _, _ in calls):
+            cfg["exchange"] = ("one-shot peer-memory all-gather (ql_peer_allgather_cols_dev)"
+                               if exchange is not None else "NCCL all_gather_into_tensor")
         line = {
             "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "s8xs8/u8->s32, f32 rescale",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": wl.config(world),
+            "config": cfg,
             "roofline": roofline,
             "gpu_launches": 2 * sum(1 for layer, _, M in calls if mine(layer, M)) * args.steps,
             "clocks": clock_info,
@@ -940,7 +953,10 @@ def run_ours(args):
     for layer in layers:
         layer.free()
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        if exchange is not None:
+            exchange.close()
         dist.destroy_process_group()
 
 
@@ -1162,6 +1178,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
+                    help="column-parallel output exchange at N > 1: NCCL all-gather, or the one-shot "
+                         "peer-memory all-gather of this library (ql_peer_allgather_cols_dev)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", metavar="K,N,BITS,M", default=None,

@@ -48,6 +48,11 @@ SIGNATURES = [
     ("ql_quantize_act_rmsnorm_dev", _i, [_vp, _vp, ctypes.c_float, _i, _i, _i, _vp, _sz, _vp, _vp]),
     ("ql_matmul_rmsnorm_dev", _i, [_vp, _vp, _vp, ctypes.c_float, _i, _vp, _vp]),
     ("ql_weight_concat", _i, [ctypes.POINTER(_vp), _i, ctypes.POINTER(_vp)]),
+    ("ql_peer_exchange_create", _i, [_sz, _vp, ctypes.POINTER(_vp)]),
+    ("ql_peer_exchange_connect", _i, [_vp, _i, _i, _vp]),
+    ("ql_peer_exchange_output", _vp, [_vp]),
+    ("ql_peer_allgather_cols_dev", _i, [_vp, _vp, _i, _i, _vp]),
+    ("ql_peer_exchange_destroy", _i, [_vp]),
     ("ql_weight_serialized_bytes", _sz, [_vp]),
     ("ql_weight_serialize", _i, [_vp, _vp, _sz]),
     ("ql_weight_deserialize", _i, [_vp, _sz, ctypes.POINTER(_vp)]),

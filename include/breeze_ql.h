@@ -182,6 +182,34 @@ int ql_matmul_rmsnorm_dev(void* handle, const float* dX, const float* dNormW, fl
  * ql_prepack_onnx_dev writing them before the call.  Free with i4_free. */
 int ql_weight_concat(void* const* handles, int count, void** out_handle);
 
+/* One-shot all-gather of column-parallel outputs over peer memory (no
+ * counterpart in the reference, which runs on one CPU; the multi-GPU step that
+ * replaces an NCCL all-gather of the [M, N/P] output slices at decode sizes,
+ * where the collective is latency-bound).  One process per GPU:
+ *   ql_peer_exchange_create   allocates this GPU's region (output capacity
+ *                             `bytes`, plus flags) and writes its CUDA IPC
+ *                             handle (QL_IPC_HANDLE_BYTES bytes);
+ *   ql_peer_exchange_connect  maps every peer's region, given all GPUs'
+ *                             handles in rank order (world <= 8);
+ *   ql_peer_allgather_cols_dev  every GPU stores its slice dShard [M, Nl]
+ *                             (Nl % 4 == 0, 16-byte aligned) into every GPU's
+ *                             output [M, Nl * world] over NVLink, then the
+ *                             GPUs hand-shake through the flags (each wait
+ *                             bounded at 5 s; on expiry QL_ETIMEOUT in the
+ *                             device error word).  All GPUs make the same
+ *                             sequence of calls.  The result, at
+ *                             ql_peer_exchange_output(), is complete for work
+ *                             enqueued after the call on the same stream and
+ *                             valid until this GPU's next call.  The kernels'
+ *                             arguments do not change between calls, so the
+ *                             call can be captured in a CUDA graph. */
+#define QL_IPC_HANDLE_BYTES 64
+int ql_peer_exchange_create(size_t bytes, void* ipc_handle, void** exchange);
+int ql_peer_exchange_connect(void* exchange, int rank, int world, const void* handles);
+float* ql_peer_exchange_output(void* exchange);
+int ql_peer_allgather_cols_dev(void* exchange, const float* dShard, int M, int Nl, void* stream);
+int ql_peer_exchange_destroy(void* exchange);
+
 /* ql_matmul_dev without any device allocation (no counterpart in the
  * reference, which allocates its activation scratch on every call,
  * kernel/quantized_matmul.cpp:532-534).  For callers that cannot allocate

@@ -82,3 +82,74 @@ def test_column_and_row_parallel_on_two_gpus():
     for rank, out in results.items():
         assert out["col1"] and out["col37"], (rank, out)
         assert out["row1"] <= 1e-5 and out["row37"] <= 1e-5, (rank, out)
+
+
+def _peer_worker(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        from breeze_engine_b200 import _lib as L
+        from breeze_engine_b200 import sharded
+        lib = L.load()
+        n = 64                                            # columns per GPU
+        ex = sharded.PeerExchange(37 * n * world * 4)
+        out = {"eager": True, "graph": True}
+        g = torch.Generator(device="cuda")
+        for it in range(60):                              # changing shapes and data, back-to-back calls
+            M = (1, 16, 37)[it % 3]
+            g.manual_seed(1000 * it + rank)
+            local = torch.randn((M, n), generator=g, device="cuda")
+            got = ex.gather(local).clone()
+            want = sharded.gather_columns(local)
+            out["eager"] &= bool(torch.equal(got.view(torch.int32), want.view(torch.int32)))
+        # captured once, replayed with new data each time
+        local = torch.zeros((16, n), device="cuda")
+        ex.gather(local)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            res = ex.gather(local)
+        for it in range(20):
+            g.manual_seed(5000 + 100 * it + rank)
+            local.copy_(torch.randn((16, n), generator=g, device="cuda"))
+            graph.replay()
+            got = res.clone()
+            want = sharded.gather_columns(local)
+            out["graph"] &= bool(torch.equal(got.view(torch.int32), want.view(torch.int32)))
+        torch.cuda.synchronize()
+        del graph
+        out["device_error"] = lib.ql_device_error(1)
+        q.put((rank, out))
+    finally:
+        if ex is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_peer_allgather_matches_nccl_on_two_gpus():
+    """ql_peer_allgather_cols_dev gives NCCL's all-gather bit for bit, over many
+    back-to-back calls of changing shape, eagerly and replayed from a CUDA graph,
+    with no bounded wait expiring."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, out in results.items():
+        assert out["eager"] and out["graph"] and out["device_error"] == 0, (rank, out)
