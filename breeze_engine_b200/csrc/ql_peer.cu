@@ -10,15 +10,14 @@
 // Region of one GPU (one cudaMalloc, exported as one IPC handle):
 //   [0, 256)            flags: word q = the last epoch GPU q posted here
 //   [256, 256 + bytes)  the full [M, N] fp32 output, written by all GPUs
-// Per call, with e = 2 * calls + 1 (a device counter, so CUDA-graph replays
-// use the right value without changing kernel arguments):
-//   put kernel   every CTA posts e ("ready": this GPU's readers of the previous
-//                result ran before this launch, in stream order) to every peer,
-//                waits until every peer posted >= e, stores its share of the
-//                slice into every peer's buffer; the last CTA to finish fences
-//                at system scope and posts e + 1 ("done").
-//   wait kernel  one warp waits until every peer posted >= e + 1 and advances
-//                the counter; the result is complete for the next kernel.
+// One kernel per call, with e = 2 * calls + 1 (a device counter, so CUDA-graph
+// replays use the right value without changing kernel arguments): every CTA
+// posts e ("ready": this GPU's readers of the previous result ran before this
+// launch, in stream order) to every peer, waits until every peer posted >= e,
+// and stores its share of the slice into every peer's buffer; the last CTA to
+// finish fences at system scope, posts e + 1 ("done"), waits until every peer
+// posted >= e + 1 and advances the counter, so the result is complete when the
+// kernel ends.
 // Every wait is bounded (5 s): on expiry the device error word gets
 // QL_ETIMEOUT and the kernel returns, so a missing peer cannot hang a GPU.
 #include <algorithm>
@@ -62,7 +61,7 @@ struct Exchange {
 struct PeerArgs {
     uint8_t* peer[MAX_PEERS];
     int P, rank;
-    const unsigned int* counter;
+    unsigned int* counter;
     unsigned int* blocks_done;
     int* err;
 };
@@ -120,24 +119,28 @@ __global__ void __launch_bounds__(PUT_THREADS) peer_put_kernel(const float* __re
                 *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.peer[p] + FLAG_BYTES) + off) = v;
         }
     }
-    // the last CTA to finish posts "done" once every CTA's stores are fenced
-    __threadfence_system();
+    // The CTA's stores are ordered before its thread 0 by the barrier; thread 0
+    // fences at system scope and counts the CTA done.  The last CTA posts
+    // "done" to every peer, its first warp waits for every peer's "done" and
+    // advances the call counter (every other CTA has read it by then).
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned int prev = atomicAdd(a.blocks_done, 1u);
-        if (prev == gridDim.x - 1) {
-            *a.blocks_done = 0u;
+    if (threadIdx.x < 32) {
+        unsigned int last = 0;
+        if (threadIdx.x == 0) {
             __threadfence_system();
-            for (int p = 0; p < a.P; ++p) post_flag(a.peer[p], a.rank, e + 1u);
+            last = atomicAdd(a.blocks_done, 1u) == gridDim.x - 1 ? 1u : 0u;
+            if (last) {
+                *a.blocks_done = 0u;
+                __threadfence_system();
+                for (int p = 0; p < a.P; ++p) post_flag(a.peer[p], a.rank, e + 1u);
+            }
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            wait_flags(a.peer[a.rank], a.P, e + 1u, a.err);
+            if (threadIdx.x == 0) *a.counter = (e + 1u) / 2u;
         }
     }
-}
-
-__global__ void peer_wait_kernel(PeerArgs a) {
-    const unsigned int e = 2u * *a.counter + 2u;
-    wait_flags(a.peer[a.rank], a.P, e, a.err);
-    __syncwarp();
-    if (threadIdx.x == 0) *const_cast<unsigned int*>(a.counter) += 1u;
 }
 
 int status_of(cudaError_t e) {
@@ -257,12 +260,7 @@ QL_API int ql_peer_allgather_cols_dev(void* exchange, const float* dShard, int M
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, peer_put_kernel, dShard, M, Nl, a);
-    if (e == cudaSuccess) {
-        peer_wait_kernel<<<1, 32, 0, s>>>(a);
-        e = cudaGetLastError();
-    }
-    return status_of(e);
+    return status_of(cudaLaunchKernelEx(&cfg, peer_put_kernel, dShard, M, Nl, a));
 }
 
 QL_API int ql_peer_exchange_destroy(void* exchange) {
