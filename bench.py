@@ -3,7 +3,7 @@
 
 Workloads (``--workload``):
 
-* ``decode`` (default): the INT8 decode GEMV sweep --
+* ``decode`` (default; configs[1] of the benchmark spec): the INT8 decode GEMV sweep --
   batch M in {1, 4, 8, 16} x (K, N) in {(4096, 12288), (12288, 4096),
   (4096, 151936)}, weights N(0, 0.02) packed to INT8 per output channel,
   activations N(0, 1) quantized to two-pass INT16.  One *step* is the 12 calls
@@ -14,8 +14,10 @@ Workloads (``--workload``):
   tokens, K = 5120, N = 17408, weights N(0, 0.02) RTN-packed to INT4 with fp16
   scales, activations N(0, 1) with 1% of the channels scaled x20 (outliers),
   two-pass INT16.  One step is the 3 calls.  ``value`` is INT8 tera-operations
-  per second counted as BASELINE.md does: ``4*M*N*K`` per call (two INT8
-  passes of 2*M*N*K each).
+  per second counted as the headline metric does: ``4*M*N*K`` per call (two
+  INT8 passes of 2*M*N*K each).  The default ``decode`` line also carries this
+  workload's measurement under ``secondary.prefill`` (``--no-secondary`` skips
+  it), so one driver run measures both halves of the metric.
 * ``mlp_front``: the front of a Qwen3.5-27B MLP block at decode batch sizes
   (M in {1, 4, 8, 16}; H = 5120, intermediate 17408, INT4 with fp16 scales):
   the RMSNorm fused into the activation quantizer, then one decode launch over
@@ -25,9 +27,13 @@ Workloads (``--workload``):
   reference's own rmsnorm and two i4_matmul per M.  ``--gpus P`` runs P
   replicas.
 
-With ``--gpus P`` every layer is column-parallel (N/P per GPU) and the output
-shards are NCCL-all-gathered: total work is fixed, so scaling is "strong".
-Other BASELINE configs are parity-test cases (tests/), not bench lines.
+With ``--gpus P`` (total work fixed, "strong" scaling) the decode sweep
+column-shards the LM head (N/P per GPU, NCCL all-gather of the output; or the
+library's peer-memory all-gather with ``--exchange peer``) and deals the calls
+of the two 50 MB layers round-robin over the GPUs as whole, independent calls;
+``prefill`` column-shards its layer; ``sharded_m1`` / ``sharded_m2048``
+(configs[4]) shard one layer column-parallel and one row-parallel.  Every
+other config is also a parity-test case (tests/).
 
 Inputs stay resident in HBM; every call streams its weights from HBM because
 each layer is packed into several copies that are rotated (the working set of
@@ -53,13 +59,15 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+DATA = ("synthetic: seeded N(0,0.02) weights RTN-packed to MatMulNBits (fp16 scales), "
+        "seeded N(0,1) activations; identical in both arms")
 FALLBACK_HBM_GBS = 6650.0
 NOMINAL_INT8_TOPS = 4500.0           # dense INT8, B200 (NVIDIA's figure without sparsity)
 SMS = 148
 
 
 def alg_bytes(M, K, N, bits):
-    """Algorithmic bytes of one call (BASELINE.md decode formula, fp16 scales)."""
+    """Algorithmic bytes of one call (the decode metric's formula, fp16 scales)."""
     return N * K * bits // 8 + 2 * N * (K // 32) + 4 * M * K + 4 * M * N
 
 
@@ -228,16 +236,20 @@ class Layer:
 
 # ------------------------------------------------------------------ workloads
 
-def _outlier_acts(M, K, seed):
+def _outlier_acts(M, K, seed, dev="cuda"):
     """N(0, 1) activations with 1% of the channels scaled x20 (the outlier
     channels exercise the INT16 hi/lo split); seeded, on the device."""
     import torch
-    g = torch.Generator(device="cuda")
+    g = torch.Generator(device=dev)
     g.manual_seed(seed)
-    a = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
-    ch = torch.randperm(K, generator=g, device="cuda")[: max(1, K // 100)]
+    a = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32)
+    ch = torch.randperm(K, generator=g, device=dev)[: max(1, K // 100)]
     a[:, ch] *= 20.0
     return a
+
+
+def _to_host(acts):
+    return {k: v.cpu().numpy() for k, v in acts.items()}
 
 
 class DecodeWorkload:
@@ -252,7 +264,7 @@ class DecodeWorkload:
     # Layers of at least this many weight bytes are column-sharded across the
     # GPUs (NCCL all-gather of the outputs); smaller layers stay whole and their
     # calls -- independent units of the sweep -- are dealt round-robin to the
-    # GPUs, so only sharded shapes have a collective (BASELINE.json north_star).
+    # GPUs, so only sharded shapes have a collective.
     SHARD_BYTES = 256 << 20
 
     @classmethod
@@ -286,12 +298,7 @@ class DecodeWorkload:
                 copies = int(min(len(self.Ms), max(1, -(-2 * L2_BYTES // shard))))
                 layer = Layer(lib, K, N, self.bits, world, rank, 1000 + i, copies)
             layers.append(layer)
-        g = torch.Generator(device="cuda")
-        g.manual_seed(7)
-        acts = {}
-        for K in sorted({k for k, _ in self.shapes}):
-            for M in self.Ms:
-                acts[(M, K)] = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
+        acts = self.make_acts("cuda")
         calls = []
         for layer in layers:
             for j, M in enumerate(self.Ms):
@@ -331,10 +338,24 @@ class DecodeWorkload:
                                 f"LM head (661 MB) column-parallel N/{world} + NCCL all-gather; the 50 MB "
                                 f"layers whole, their 8 calls dealt round-robin over the {world} GPUs")}
 
-    def cpu_calls(self):
-        """(K, N, bits, Ms) of the reference timing; `samples` steps of these."""
-        return [(K, N, self.bits, self.Ms) for K, N in self.shapes]
+    def make_acts(self, dev):
+        import torch
+        g = torch.Generator(device=dev)
+        g.manual_seed(7)
+        acts = {}
+        for K in sorted({k for k, _ in self.shapes}):
+            for M in self.Ms:
+                acts[(M, K)] = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32)
+        return acts
 
+    def host_acts(self):
+        return _to_host(self.make_acts(_gen_device()))
+
+    def cpu_calls(self):
+        """(K, N, bits, Ms, weight seed) of the bounded reference sample: the full sweep."""
+        return [(K, N, self.bits, self.Ms, 1000 + i) for i, (K, N) in enumerate(self.shapes)]
+
+    ref_calls = cpu_calls
     cpu_sample = "full decode sweeps (12 i4_matmul calls each)"
 
 
@@ -347,9 +368,15 @@ class PrefillWorkload:
 
     def build(self, lib, world, rank):
         layer = Layer(lib, self.K, self.N, self.bits, world, rank, 3000, len(self.Ms))
-        acts = {(M, self.K): _outlier_acts(M, self.K, 11 + M) for M in self.Ms}
+        acts = self.make_acts("cuda")
         calls = [(layer, layer.handles[j % len(layer.handles)], M) for j, M in enumerate(self.Ms)]
         return [layer], acts, calls
+
+    def make_acts(self, dev):
+        return {(M, self.K): _outlier_acts(M, self.K, 11 + M, dev) for M in self.Ms}
+
+    def host_acts(self):
+        return _to_host(self.make_acts(_gen_device()))
 
     def step_amount(self, calls):
         return sum(prefill_ops(M, layer.K, layer.N) for layer, _, M in calls)
@@ -365,7 +392,7 @@ class PrefillWorkload:
         # 32-wide block one K = 64 FP16 MMA (h and l/256 planes) = exactly the
         # 4*M*N*K operations counted here, on the FP16 tensor pipe.  Its roofline
         # is the measured dense 16-bit tensor peak; the INT8 peak (the metric
-        # BASELINE.json names) is reported beside it.
+        # headline metric names) is reported beside it.
         f16_peak, f16_kind = measured_tensor_peak()
         int8_peak, int8_kind = measure_int8_tops()
         out = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(f16_peak, 1),
@@ -391,7 +418,10 @@ class PrefillWorkload:
                 "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
 
     def cpu_calls(self):
-        return [(self.K, self.N, self.bits, [128])]
+        return [(self.K, self.N, self.bits, [128], 3000)]
+
+    def ref_calls(self):
+        return [(self.K, self.N, self.bits, self.Ms, 3000)]
 
     cpu_sample = "i4_matmul calls at M=128 (the smallest prefill size)"
 
@@ -453,8 +483,16 @@ class LayerSetWorkload(_OpsOrBytes):
                 "timing": "CUDA graph of one step (7 quantize+matmul calls), CUDA events",
                 "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
 
+    def host_acts(self):
+        dev = _gen_device()
+        Ks = sorted({K for _, K, _ in self.shapes})
+        return _to_host({(m, K): _outlier_acts(m, K, 21 + K, dev) for m in {self.M, min(self.M, 128)} for K in Ks})
+
     def cpu_calls(self):
-        return [(K, N, self.bits, [min(self.M, 128)]) for _, K, N in self.shapes]
+        return [(K, N, self.bits, [min(self.M, 128)], 4000 + i) for i, (_, K, N) in enumerate(self.shapes)]
+
+    def ref_calls(self):
+        return [(K, N, self.bits, [self.M], 4000 + i) for i, (_, K, N) in enumerate(self.shapes)]
 
     @property
     def cpu_sample(self):
@@ -491,9 +529,17 @@ class ShardedWorkload(_OpsOrBytes):
                 "parallelism": (f"P={world}: column-parallel + NCCL all-gather, row-parallel + NCCL reduce-scatter"
                                 if world > 1 else "P=1 (no collective)")}
 
+    def host_acts(self):
+        dev = _gen_device()
+        return _to_host({(m, K): _outlier_acts(m, K, seed, dev) for m in {self.M, min(self.M, 128)}
+                         for K, seed in ((8192, 31), (65536, 32))})
+
     def cpu_calls(self):
         m = min(self.M, 128)
-        return [(8192, 65536, self.bits, [m]), (65536, 8192, self.bits, [m])]
+        return [(8192, 65536, self.bits, [m], 5000), (65536, 8192, self.bits, [m], 5001)]
+
+    def ref_calls(self):
+        return [(8192, 65536, self.bits, [self.M], 5000), (65536, 8192, self.bits, [self.M], 5001)]
 
     @property
     def cpu_sample(self):
@@ -736,9 +782,7 @@ def run_ours(args):
     import torch.distributed as dist
     from breeze_engine_b200 import _lib as L
     from breeze_engine_b200 import backend
-    from breeze_engine_b200.sharded import gather_columns, reduce_partials
 
-    wl = WORKLOADS[args.workload]()
     rank, local_rank, world = dist_env()
     torch.cuda.set_device(local_rank)
     if world > 1:
@@ -747,6 +791,30 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local_rank))
     lib = L.load()
     backend.set_hi_prec(True)
+    line = _measure(args, WORKLOADS[args.workload](), lib, rank, local_rank, world)
+    # The headline metric names both halves of the path: the default decode
+    # line also carries configs[2]'s prefill GEMM, measured the same way.
+    if args.workload == "decode" and not args.no_secondary:
+        sec = _measure(args, PrefillWorkload(), lib, rank, local_rank, world)
+        if rank == 0:
+            keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "e2e",
+                    "cpu_baseline", "gpu_launches", "clocks")
+            line["secondary"] = {"prefill": {k: sec[k] for k in keep if k in sec}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _measure(args, wl, lib, rank, local_rank, world):
+    """One workload on this rank: the timed step (value), the kernel-only
+    pass (roofline), the host-pointer pass (e2e) and, on rank 0 at N = 1, the
+    reference's CPU path (cpu_baseline).  Returns the JSON line on rank 0."""
+    import torch
+    import torch.distributed as dist
+    from breeze_engine_b200.sharded import gather_columns, reduce_partials
 
     layers, acts, calls = wl.build(lib, world, rank)
     owners = getattr(wl, "owners", {})
@@ -925,19 +993,20 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(wl, samples=2)
+        cpu = cpu_baseline(wl)
 
+    line = None
     if rank == 0:
         cfg = wl.config(world)
         if world > 1 and any(layer.mode == "col" for layer, _, _ in calls):
             cfg["exchange"] = ("one-shot peer-memory all-gather (ql_peer_allgather_cols_dev)"
                                if exchange is not None else "NCCL all_gather_into_tensor")
         line = {
-            "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
+            "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "impl": "ours", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "s8xs8/u8->s32, f32 rescale",
-            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "data": DATA,
             "config": cfg,
             "roofline": roofline,
             "gpu_launches": 2 * sum(1 for layer, _, M in calls if mine(layer, M)) * args.steps,
@@ -947,7 +1016,6 @@ def run_ours(args):
             line["e2e"] = e2e
         if cpu:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
 
     del graph
     for layer in layers:
@@ -955,9 +1023,9 @@ def run_ours(args):
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()
-        if exchange is not None:
-            exchange.close()
-        dist.destroy_process_group()
+    if exchange is not None:
+        exchange.close()
+    return line
 
 
 # ------------------------------------------------------------------ CPU reference
@@ -978,6 +1046,26 @@ def host_weights(K, N, bits, seed):
     return qw, sc
 
 
+def _gen_device():
+    import torch
+    return "cuda" if torch.cuda.is_available() else "cpu"
+
+
+def rtn_host_weights(K, N, bits, seed):
+    """The GPU arm's layer weights (Layer: seeded N(0, 0.02), RTN-packed by
+    quantize_matmul_nbits_torch), generated the same way and copied to host
+    memory, so both arms multiply the same MatMulNBits arrays."""
+    import torch
+    from breeze_engine_b200.quant import quantize_matmul_nbits_torch
+    dev = _gen_device()
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w = torch.randn((K, N), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+    qw, sc, _ = quantize_matmul_nbits_torch(w, bits=bits, per_channel=(bits == 8))
+    del w
+    return qw.cpu().numpy(), sc.cpu().numpy()
+
+
 def _reference_lib():
     from oracle.oracle import REF_SO, Reference
     if not os.path.exists(REF_SO):
@@ -988,19 +1076,20 @@ def _reference_lib():
 
 
 class _RefCalls:
-    """The reference's i4_matmul over a list of (K, N, bits, Ms), host buffers."""
+    """The reference's i4_matmul over the workload's calls, host buffers: the
+    GPU arm's weights (rtn_host_weights with the layer's seed) and activations
+    (the workload's own generator), copied to host memory."""
 
-    def __init__(self, ref, spec, threads):
+    def __init__(self, ref, wl, spec, threads):
         self.ref = ref
         self.handles = []
-        for i, (K, N, bits, Ms) in enumerate(spec):
-            qw, sc = host_weights(K, N, bits, 100 + i)
+        for K, N, bits, Ms, seed in spec:
+            qw, sc = rtn_host_weights(K, N, bits, seed)
             self.handles.append((K, N, bits, Ms, ref.prepack(qw, sc, None, K, N, bits)))
             del qw
-        rng = np.random.default_rng(7)
-        self.acts = {(M, K): rng.standard_normal((M, K)).astype(np.float32)
-                     for K, _, _, Ms in spec for M in Ms}
-        self.outs = {(M, N): np.empty((M, N), np.float32) for _, N, _, Ms in spec for M in Ms}
+        acts = wl.host_acts()
+        self.acts = {(M, K): acts[(M, K)] for K, _, _, Ms, _ in spec for M in Ms}
+        self.outs = {(M, N): np.empty((M, N), np.float32) for _, N, _, Ms, _ in spec for M in Ms}
         ref.lib.i4_set_threads(threads)
         ref.lib.i4_set_hi_prec(1)
 
@@ -1020,26 +1109,50 @@ class _RefCalls:
             self.ref.free(h)
 
 
-def cpu_baseline(wl, samples=2):
-    """The reference i4_matmul (OpenMP, all host threads) on a bounded sample."""
+def _median_sample(step, samples, warmup=2):
+    """Median wall time of `samples` calls of step() after `warmup` calls."""
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def _host_desc(threads):
+    model = ""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    numa = len([d for d in os.listdir("/sys/devices/system/node") if d.startswith("node")]) \
+        if os.path.isdir("/sys/devices/system/node") else 1
+    return f"{model or 'unknown CPU'}, {os.cpu_count()} logical CPUs, {numa} NUMA node(s), {threads} OpenMP threads"
+
+
+def cpu_baseline(wl, samples=10):
+    """The reference i4_matmul (OpenMP, all host threads) on a bounded sample:
+    the median of `samples` timed steps after 2 warm-ups, on the GPU arm's
+    weights and activations."""
     os.environ.setdefault("OMP_PROC_BIND", "spread")
     os.environ.setdefault("OMP_PLACES", "cores")
     ref, why = _reference_lib()
     if ref is None:
         return {"value": None, "unit": wl.unit, "cores": 0, "kind": "reference", "sample": why}
     threads = os.cpu_count() or 1
-    rc = _RefCalls(ref, wl.cpu_calls(), threads)
-    rc.step()
-    t0 = time.perf_counter()
-    for _ in range(samples):
-        rc.step()
-    dt = time.perf_counter() - t0
-    value = wl.value(rc.amount(wl) * samples, dt)
+    rc = _RefCalls(ref, wl, wl.cpu_calls(), threads)
+    dt = _median_sample(rc.step, samples)
+    value = wl.value(rc.amount(wl), dt)
     rc.free()
     return {"value": round(value, 4 if wl.unit == "TOPS" else 2), "unit": wl.unit, "cores": threads,
-            "kind": "reference", "ms_per_step": round(dt / samples * 1e3, 2),
-            "sample": f"{samples} x {wl.cpu_sample} after 1 warm-up, set_hi_prec(1), "
-                      f"OpenMP {threads} threads, OMP_PROC_BIND=spread"}
+            "kind": "reference", "ms_per_step": round(dt * 1e3, 2),
+            "sample": f"median of {samples} x {wl.cpu_sample} after 2 warm-ups, set_hi_prec(1), "
+                      f"OMP_PROC_BIND=spread; host: {_host_desc(threads)}"}
 
 
 class _RefMlpFront:
@@ -1116,9 +1229,8 @@ def run_reference(args):
     if wl.name == "mlp_front":
         rc = _RefMlpFront(ref, wl, threads)
     else:
-        spec = ([(wl.K, wl.N, wl.bits, wl.Ms)] if wl.name == "prefill" else
-                [(K, N, b, [wl.M]) for K, N, b, _ in wl.cpu_calls()] if hasattr(wl, "M") else wl.cpu_calls())
-        rc = _RefCalls(ref, spec, threads)
+        # the workload's full step (every call at its own M), on the GPU arm's data
+        rc = _RefCalls(ref, wl, wl.ref_calls(), threads)
     for _ in range(args.warmup):
         rc.step()
     t0 = time.perf_counter()
@@ -1127,19 +1239,18 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     value = wl.value(rc.amount(wl) * args.steps, dt)
     rc.free()
-    cfg = wl.config(1)
-    cfg["parallelism"] = f"host OpenMP, {threads} threads (rank 0 only)"
-    cfg.pop("timing", None)
-    cfg.pop("l2", None)
+    # the same workload description as the GPU arm's line (world as launched)
+    cfg = wl.config(world)
     line = {"metric": wl.metric, "value": round(value, 4), "unit": wl.unit, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak" if wl.name == "mlp_front" else "strong", "vs_baseline": None,
             "dtype": "u8xs8->s32 (VPDPBUSD), f32 rescale",
-            "data": "synthetic (random MatMulNBits codes, fp16 scales; N(0,1) activations)",
+            "data": DATA if wl.name != "mlp_front" else "synthetic (random MatMulNBits codes; N(0,1) rows)",
             "config": cfg,
             "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "reference",
-                             "sample": f"{args.steps} full steps after {args.warmup} warm-ups"},
+                             "sample": f"{args.steps} full steps after {args.warmup} warm-ups, rank 0 only; "
+                                       f"host: {_host_desc(threads)}"},
             "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -1183,6 +1294,8 @@ def main(argv=None):
                          "peer-memory all-gather of this library (ql_peer_allgather_cols_dev)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="decode workload: skip the configs[2] prefill measurement in `secondary`")
     ap.add_argument("--ncu-case", metavar="K,N,BITS,M", default=None,
                     help="profiling driver: pack one layer, quantize once, run the matmul kernel "
                          "4 times and exit (for ncu captures of a single launch)")

@@ -12,6 +12,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("BREEZE_B200_KERNEL", os.path.join(HERE, "libbreeze_ql.so"))
 
 QL_OK, QL_EINVAL, QL_ENOMEM, QL_ECUDA, QL_ETIMEOUT, QL_EDEVICE, QL_ENOTSUP, QL_ESCRATCH = range(8)
+DEFAULT_WAIT_NS = 1_000_000_000        # QL_DEFAULT_WAIT_NS of include/breeze_ql.h
+DEFAULT_PEER_WAIT_NS = 5_000_000_000   # QL_DEFAULT_PEER_WAIT_NS
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -34,6 +36,7 @@ SIGNATURES = [
     ("ql_error_string", ctypes.c_char_p, [_i]),
     ("ql_last_cuda_error_string", ctypes.c_char_p, []),
     ("ql_device_error", _i, [_i]),
+    ("ql_set_wait_limits", _i, [ctypes.c_ulonglong, ctypes.c_ulonglong]),
     ("ql_prepack_onnx_dev", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.POINTER(_vp)]),
     ("ql_weight_info", _i, [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i),
                             ctypes.POINTER(_i), ctypes.POINTER(ctypes.c_ulonglong)]),

@@ -64,6 +64,30 @@ def get_hi_prec():
     return bool(L.load().ql_get_hi_prec())
 
 
+def device_error(clear=True):
+    """Synchronise the current CUDA device and return its device error word:
+    0, or the code (``QL_ETIMEOUT``) a kernel recorded when one of its bounded
+    waits gave up.  ``clear`` resets it.  The synchronous NumPy path of
+    :func:`matmul` checks it after every call; callers of the asynchronous
+    torch path check it here after they synchronise."""
+    return int(L.load().ql_device_error(1 if clear else 0))
+
+
+def check_device(what="device"):
+    """Raise :class:`breeze_engine_b200._lib.QLError` when the device error
+    word is set (and clear it)."""
+    code = device_error(clear=True)
+    if code:
+        raise L.QLError(code, what)
+
+
+def set_wait_limits(wait_ns=0, peer_wait_ns=0):
+    """Limits of the bounded device waits on the current device (0 keeps one):
+    kernel-internal waits (1 s by default) and waits on another GPU's flags in
+    the peer exchange (5 s by default)."""
+    L.check(L.load().ql_set_wait_limits(int(wait_ns), int(peer_wait_ns)), "set_wait_limits")
+
+
 def _p(a):
     return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
 
@@ -167,8 +191,10 @@ def matmul(handle, a2d, N):
     """``a2d`` fp32 ``[M, K]`` -> fp32 ``[M, N]`` (``breeze/cpu_backend.py:230-237``).
 
     NumPy in, NumPy out (synchronous, through the reference-compatible
-    ``i4_matmul``), or torch CUDA tensor in, CUDA tensor out (asynchronous on
-    the current stream, through ``ql_matmul_dev_ws``).
+    ``i4_matmul``, which also reads the device error word: a kernel wait that
+    gave up raises :class:`~breeze_engine_b200._lib.QLError`), or torch CUDA
+    tensor in, CUDA tensor out (asynchronous on the current stream, through
+    ``ql_matmul_dev_ws``; check :func:`check_device` after synchronising).
     """
     lib = L.load()
     hN, hK, _, hdev, _ = weight_info(handle)

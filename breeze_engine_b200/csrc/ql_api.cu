@@ -25,7 +25,8 @@
 
 namespace ql {
 
-__device__ int g_device_error_word = 0;
+// The device control block (ql_common.cuh): error word and wait limits.
+__device__ DeviceCtl g_device_ctl = {0, 0, WAIT_LIMIT_NS, PEER_WAIT_LIMIT_NS};
 
 namespace {
 
@@ -45,6 +46,7 @@ struct DeviceState {
     size_t ws_bytes = 0;
     cudaStream_t copy_stream = nullptr;   // i4_matmul: output copies overlapping the matmul
     cudaEvent_t chunk_done[8] = {};       // i4_matmul: one per output column chunk
+    int* host_err = nullptr;              // pinned copy of the device error word (i4_matmul)
 };
 DeviceState g_dev[MAX_DEVICES];
 
@@ -213,7 +215,7 @@ int* device_error_word() {
     if (!st) return nullptr;
     if (!st->err_word) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) {
+        if (cudaGetSymbolAddress(&p, g_device_ctl) != cudaSuccess) {
             cudaGetLastError();
             return nullptr;
         }
@@ -271,6 +273,20 @@ QL_API int ql_set_prefill_kernel(int kind) {
         return set_status(QL_EINVAL);
     g_prefill_kernel.store(kind, std::memory_order_relaxed);
     return set_status(QL_OK);
+}
+
+// Limits of the bounded device waits on the current device: kernel-internal
+// waits (default 1 s) and waits on another GPU's flags (default 5 s).  0 keeps
+// a limit as it is.  Serialise with running calls.
+QL_API int ql_set_wait_limits(unsigned long long wait_ns, unsigned long long peer_wait_ns) {
+    int* w = device_error_word();
+    if (!w) return set_status(QL_ECUDA);
+    DeviceCtl* ctl = reinterpret_cast<DeviceCtl*>(w);
+    cudaError_t e = cudaSuccess;
+    if (wait_ns) e = cudaMemcpy(&ctl->wait_ns, &wait_ns, sizeof(wait_ns), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && peer_wait_ns)
+        e = cudaMemcpy(&ctl->peer_wait_ns, &peer_wait_ns, sizeof(peer_wait_ns), cudaMemcpyHostToDevice);
+    return cuda_status(e);
 }
 
 QL_API const char* ql_error_string(int code) {
@@ -762,11 +778,10 @@ QL_API int ql_weight_concat(void* const* handles, int count, void** out_handle) 
 // ------------------------------------------------------------------ no-allocation variant
 //
 // Some callers cannot allocate device memory at the time they run a layer:
-// code that is being captured into a CUDA graph (cudaMalloc is not allowed
-// during stream capture), serving runtimes whose allocator owns all of HBM
-// (weights and KV cache are reserved up front and nothing else may allocate),
-// and per-token decode loops that cannot pay for an allocation or for the
-// device-wide synchronisation that freeing one implies.  For them,
+// serving runtimes whose allocator owns all of HBM (weights and KV cache are
+// reserved up front and nothing else may allocate), and per-token decode loops
+// that cannot pay for an allocation or for the device-wide synchronisation
+// that freeing one implies.  For them,
 // ql_matmul_dev_noalloc keeps the quantized activations in a fixed scratch
 // array compiled into this library instead of a workspace.
 //
@@ -839,6 +854,17 @@ QL_API int ql_quantize_dev(const float* dA, int M, int K, uint8_t* dHi, uint8_t*
 // 128 columns, so every chunk is whole GEMM tiles and decode row groups); each
 // chunk's matmul runs on the call's stream and its device -> host copy starts
 // on a second stream as soon as it is done, overlapping the next chunk.
+// After a synchronous call: a bounded wait of one of its kernels gave up if the
+// error word (copied to host_err behind the call's work) is set.  The call then
+// reports that code (QL_ETIMEOUT) instead of QL_OK, and the word is cleared so
+// the next call starts clean.
+static int take_device_error(DeviceState* st, int* err_word, cudaStream_t s) {
+    const int v = st->host_err ? *st->host_err : 0;
+    if (!v) return set_status(QL_OK);
+    if (err_word && cudaMemsetAsync(err_word, 0, sizeof(int), s) == cudaSuccess) cudaStreamSynchronize(s);
+    return set_status(v);
+}
+
 static int output_chunks(int M, int N) {
     const size_t bytes = static_cast<size_t>(M) * N * 4;
     int chunks = static_cast<int>(std::min<size_t>(8, bytes / (512 * 1024)));
@@ -881,13 +907,26 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
         cuda_status(e);
         return;
     }
+    int* err_word = device_error_word();
+    if (!st->host_err) {
+        e = cudaHostAlloc(reinterpret_cast<void**>(&st->host_err), sizeof(int), cudaHostAllocDefault);
+        if (e != cudaSuccess) {
+            st->host_err = nullptr;
+            cuda_status(e);
+            return;
+        }
+    }
+    *st->host_err = 0;
     const int chunks = output_chunks(M, w->N);
     if (chunks == 1) {
         int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
         if (rc != QL_OK) return;
         e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && err_word)
+            e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-        cuda_status(e);
+        if (e == cudaSuccess) take_device_error(st, err_word, s);
+        else cuda_status(e);
         return;
     }
     if (!st->copy_stream) {
@@ -918,10 +957,13 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
             e = cudaMemcpy2DAsync(C + n0, static_cast<size_t>(w->N) * 4, dC + n0, static_cast<size_t>(w->N) * 4,
                                   static_cast<size_t>(nc) * 4, M, cudaMemcpyDeviceToHost, st->copy_stream);
     }
+    if (e == cudaSuccess && rc == QL_OK && err_word)
+        e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
     // both streams drain before returning (also after a failure, so no copy is in flight)
     cudaError_t e1 = cudaStreamSynchronize(s);
     cudaError_t e2 = cudaStreamSynchronize(st->copy_stream);
     if (rc != QL_OK) return;
     if (e == cudaSuccess) e = (e1 != cudaSuccess) ? e1 : e2;
-    cuda_status(e);
+    if (e == cudaSuccess) take_device_error(st, err_word, s);
+    else cuda_status(e);
 }

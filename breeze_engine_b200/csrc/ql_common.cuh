@@ -39,12 +39,34 @@ enum : int {
     QL_ESCRATCH = 7,      // request needs more than the fixed scratch of the no-alloc entry point
 };
 
-// ---------------------------------------------------------------- device error word
-// One int per device (defined in ql_api.cu, passed to kernels as a pointer).
-// Kernels record the first failure here instead of trapping; the host reads
-// and clears it through ql_device_error().
+// ---------------------------------------------------------------- device control block
+// One per device (defined in ql_api.cu).  Kernels get a pointer to its first
+// member, the device error word: they record the first failure there instead
+// of trapping, and the host reads and clears it (ql_device_error, and the
+// synchronous entry points after every call).  The same block holds the
+// limits of the bounded waits, settable from the host (ql_set_wait_limits).
+struct DeviceCtl {
+    int err;                          // device error word (0 = none)
+    int pad;
+    unsigned long long wait_ns;       // limit of a kernel-internal wait
+    unsigned long long peer_wait_ns;  // limit of a wait on another GPU's flag
+};
+constexpr unsigned long long WAIT_LIMIT_NS = 1000000000ull;        // 1 s (default)
+constexpr unsigned long long PEER_WAIT_LIMIT_NS = 5000000000ull;   // 5 s (default)
+
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
+}
+
+// The wait limits in force (read once per wait that did not succeed at once).
+__device__ __forceinline__ uint64_t wait_limit(const int* err) {
+    return err ? *reinterpret_cast<const volatile unsigned long long*>(&reinterpret_cast<const DeviceCtl*>(err)->wait_ns)
+               : WAIT_LIMIT_NS;
+}
+__device__ __forceinline__ uint64_t peer_wait_limit(const int* err) {
+    return err ? *reinterpret_cast<const volatile unsigned long long*>(
+                     &reinterpret_cast<const DeviceCtl*>(err)->peer_wait_ns)
+               : PEER_WAIT_LIMIT_NS;
 }
 
 // ---------------------------------------------------------------- shared-memory helpers
@@ -106,17 +128,16 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Bounded wait: gives up after WAIT_LIMIT_NS of wall time, records QL_ETIMEOUT
-// in the device error word and returns false, so no wait in these kernels can
-// spin forever.
-constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // 1 s
-
+// Bounded wait: gives up after the device's wait limit (1 s unless set by
+// ql_set_wait_limits) of wall time, records QL_ETIMEOUT in the device error
+// word and returns false, so no wait in these kernels can spin forever.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
+    const uint64_t limit = wait_limit(err);
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > WAIT_LIMIT_NS) break;
+        if (global_ns() - t0 > limit) break;
     }
     record_error(err, QL_ETIMEOUT);
     return false;

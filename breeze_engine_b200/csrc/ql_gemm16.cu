@@ -577,17 +577,18 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
                  :: "r"(bar), "h"(static_cast<uint16_t>(3)) : "memory");
 }
 
-// Bounded wait for the pair: gives up after WAIT_LIMIT_NS, or when either CTA
+// Bounded wait for the pair: gives up after the wait limit, or when either CTA
 // raised its abort flag; on giving up it raises both flags.
 __device__ __forceinline__ bool pair_wait(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag,
                                           uint32_t peer_abort) {
     bool ok = mbar_try_wait_cluster(bar, parity, 0);
     if (!ok) {
         const uint64_t t0 = global_ns();
+        const uint64_t limit = wait_limit(err);
         while (true) {
             if (mbar_try_wait_cluster(bar, parity, 10000)) { ok = true; break; }
             if (*abort_flag) break;
-            if (global_ns() - t0 > WAIT_LIMIT_NS) {
+            if (global_ns() - t0 > limit) {
                 record_error(err, QL_ETIMEOUT);
                 *abort_flag = 1;
                 asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(peer_abort), "r"(1) : "memory");
@@ -744,7 +745,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(N_WARPS * 32, 1) gem
         {
             const uint64_t t0 = global_ns();
             while (!mbar_try_wait_cluster(smem_u32(drain), 0, 20000)) {
-                if (global_ns() - t0 > 60ull * WAIT_LIMIT_NS) { record_error(p.err, QL_ETIMEOUT); break; }
+                if (global_ns() - t0 > 60ull * wait_limit(p.err)) { record_error(p.err, QL_ETIMEOUT); break; }
             }
         }
     } else if (warp < 4 || warp >= 4 + N_EPI + X_CONV) {

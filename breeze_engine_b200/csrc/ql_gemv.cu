@@ -135,7 +135,13 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
         for (int i = 0; i < first; ++i) issue(i, false, true);
         for (int i = first; i < nst; ++i) {
             const int s = i % p.STAGES;
-            if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) return;
+            if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) {
+                // Giving up: let the copies already issued land before the CTA
+                // can exit (each slot's last issued phase; bounded waits).
+                for (int j = max(0, i - p.STAGES); j < i; ++j)
+                    if (!mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
+                return;
+            }
             issue(i, true, true);
         }
         return;

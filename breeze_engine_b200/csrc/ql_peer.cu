@@ -18,8 +18,10 @@
 // finish fences at system scope, posts e + 1 ("done"), waits until every peer
 // posted >= e + 1 and advances the counter, so the result is complete when the
 // kernel ends.
-// Every wait is bounded (5 s): on expiry the device error word gets
-// QL_ETIMEOUT and the kernel returns, so a missing peer cannot hang a GPU.
+// Every wait is bounded (the device's peer wait limit, 5 s by default): on
+// expiry the device error word gets QL_ETIMEOUT and the kernel returns, so a
+// missing peer cannot hang a GPU.  Callers check the word after their gathers
+// (ql_device_error, or the Python wrapper's check()).
 #include <algorithm>
 #include <cstring>
 
@@ -40,11 +42,12 @@ namespace {
 
 constexpr int MAX_PEERS = 8;
 constexpr size_t FLAG_BYTES = 256;
+constexpr size_t CAP_OFFSET = 128;      // inside the flag header: the region's output capacity (u64)
 constexpr int PUT_THREADS = 256;
 constexpr uint32_t EXCHANGE_MAGIC = 0x51504558u;   // "QPEX"
 // Peers run on other GPUs driven by other processes, whose launches can lag
-// this one's by more than a kernel-internal wait: allow 5 s before giving up.
-constexpr uint64_t PEER_WAIT_LIMIT_NS = 5000000000ull;
+// this one's by more than a kernel-internal wait: the flag waits use the
+// device's peer limit (5 s unless set by ql_set_wait_limits).
 // The public header states the handle size as QL_IPC_HANDLE_BYTES = 64.
 static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
 
@@ -84,8 +87,9 @@ __device__ bool wait_flags(const uint8_t* region, int P, unsigned int e, int* er
     bool ok = true;
     if (q < P) {
         const uint64_t t0 = global_ns();
+        const uint64_t limit = peer_wait_limit(err);
         while (static_cast<int>(read_flag(region, q) - e) < 0) {
-            if (global_ns() - t0 > PEER_WAIT_LIMIT_NS) {
+            if (global_ns() - t0 > limit) {
                 record_error(err, QL_ETIMEOUT);
                 ok = false;
                 break;
@@ -171,6 +175,10 @@ QL_API int ql_peer_exchange_create(size_t bytes, void* ipc_handle, void** out) {
     void* ctr = nullptr;
     if (e == cudaSuccess) e = cudaMalloc(&region, FLAG_BYTES + bytes);
     if (e == cudaSuccess) e = cudaMemset(region, 0, FLAG_BYTES + bytes);
+    // the capacity, for peers to read at connect time (flags use bytes 0..31)
+    const unsigned long long cap = bytes;
+    if (e == cudaSuccess) e = cudaMemcpy(static_cast<uint8_t*>(region) + CAP_OFFSET, &cap, sizeof(cap),
+                                         cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMalloc(&ctr, 2 * sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemset(ctr, 0, 2 * sizeof(unsigned int));
     cudaIpcMemHandle_t h;
@@ -216,6 +224,20 @@ QL_API int ql_peer_exchange_connect(void* exchange, int rank, int world, const v
         }
         x->peer[q] = static_cast<uint8_t*>(p);
     }
+    // Every GPU stores into every region: the usable capacity is the smallest.
+    size_t cap_min = x->bytes;
+    for (int q = 0; q < world; ++q) {
+        if (q == rank) continue;
+        unsigned long long cap = 0;
+        const cudaError_t e = cudaMemcpy(&cap, x->peer[q] + CAP_OFFSET, sizeof(cap), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) {
+            for (int r = 0; r < world; ++r)
+                if (r != rank && x->peer[r]) cudaIpcCloseMemHandle(x->peer[r]);
+            return status_of(e);
+        }
+        cap_min = std::min<size_t>(cap_min, cap);
+    }
+    x->bytes = cap_min;
     x->rank = rank;
     x->world = world;
     return QL_OK;

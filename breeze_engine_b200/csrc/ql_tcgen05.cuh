@@ -67,12 +67,13 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
+    const uint64_t limit = wait_limit(err);
     while (true) {
         // suspended until the phase completes (or 10 us pass), so idle roles
         // take no issue slots from the epilogue
         if (mbar_try_wait_sleep(bar, parity, 10000)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > WAIT_LIMIT_NS) break;
+        if (global_ns() - t0 > limit) break;
     }
     record_error(err, QL_ETIMEOUT);
     *abort_flag = 1;

@@ -2,7 +2,7 @@
 
 One process per GPU, ``torch.distributed`` with NCCL over NVLink/NVSwitch.
 The reference has no multi-device path; this shards one MatMulNBits layer the
-two ways BASELINE asks for:
+two ways the benchmark spec asks for:
 
 * **Column-parallel** (output features N split, ``N % (16 P) == 0``): rank r
   packs output rows ``[r N/P, (r+1) N/P)``, computes ``C[:, N_r]`` from the
@@ -171,8 +171,14 @@ class PeerExchange:
         self.out_ptr = self.lib.ql_peer_exchange_output(self.x)
         self._torch = torch
 
-    def gather(self, local):
-        """Full ``[M, N]`` from this GPU's ``[M, N/P]`` slice (contiguous fp32, CUDA)."""
+    def gather(self, local, check=False):
+        """Full ``[M, N]`` from this GPU's ``[M, N/P]`` slice (contiguous fp32, CUDA).
+
+        Asynchronous on the current stream (and capturable in a CUDA graph).
+        Its flag waits are bounded: a peer that never makes the matching call
+        leaves ``QL_ETIMEOUT`` in the device error word and a partly filled
+        output.  ``check=True`` synchronises and raises on that; otherwise call
+        :meth:`check` after synchronising (e.g. after a graph replay)."""
         torch = self._torch
         M, n = local.shape
         if local.dtype != torch.float32 or not local.is_contiguous() or local.data_ptr() % 16:
@@ -182,7 +188,18 @@ class PeerExchange:
         stream = torch.cuda.current_stream(local.device).cuda_stream
         L.check(self.lib.ql_peer_allgather_cols_dev(self.x, ctypes.c_void_p(local.data_ptr()), M, n,
                                                     ctypes.c_void_p(stream)), "peer all-gather")
-        return torch.as_tensor(_DeviceArray(self.out_ptr, (M, n * self.world)), device=local.device)
+        out = torch.as_tensor(_DeviceArray(self.out_ptr, (M, n * self.world)), device=local.device)
+        if check:
+            self.check()
+        return out
+
+    def check(self):
+        """Synchronise this GPU and raise ``QLError`` (``QL_ETIMEOUT``) if a
+        gather's bounded wait for a peer ran out since the last check; the
+        device error word is cleared."""
+        code = int(self.lib.ql_device_error(1))
+        if code:
+            raise L.QLError(code, "peer all-gather")
 
     def close(self):
         if self.x:

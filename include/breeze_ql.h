@@ -114,8 +114,22 @@ const char* ql_error_string(int code);
 const char* ql_last_cuda_error_string(void);
 
 /* Synchronises the current device and returns its device error word (set by
- * a kernel whose bounded wait gave up; 0 = none).  clear != 0 resets it. */
+ * a kernel whose bounded wait gave up; 0 = none).  clear != 0 resets it.
+ * The synchronous i4_matmul reads and clears the word after every call and
+ * reports a set word through ql_last_status() (QL_ETIMEOUT); callers of the
+ * asynchronous ql_* entry points check it with this function after they
+ * synchronise. */
 int ql_device_error(int clear);
+
+/* Limits of the bounded device waits on the current device (no counterpart in
+ * the reference, whose CPU code has no device waits): wait_ns for waits inside
+ * one kernel (default 1 s), peer_wait_ns for waits on another GPU's flags in
+ * the peer exchange (default 5 s).  0 keeps a limit unchanged.  A wait that
+ * runs out sets QL_ETIMEOUT in the device error word and its kernel returns.
+ * Serialise with running calls. */
+#define QL_DEFAULT_WAIT_NS 1000000000ull
+#define QL_DEFAULT_PEER_WAIT_NS 5000000000ull
+int ql_set_wait_limits(unsigned long long wait_ns, unsigned long long peer_wait_ns);
 
 /* Device-pointer twin of i4_prepack_onnx: the same contract with the
  * MatMulNBits arrays already in device memory, enqueued on `stream`. */
@@ -191,18 +205,23 @@ int ql_weight_concat(void* const* handles, int count, void** out_handle);
  *                             handle (QL_IPC_HANDLE_BYTES bytes);
  *   ql_peer_exchange_connect  maps every peer's region, given all GPUs'
  *                             handles in rank order (world <= 8);
+ *                             The usable capacity is the smallest of all
+ *                             GPUs' `bytes`;
  *   ql_peer_allgather_cols_dev  every GPU stores its slice dShard [M, Nl]
  *                             (Nl % 4 == 0, 16-byte aligned) into every GPU's
  *                             output [M, Nl * world] over NVLink, then the
  *                             GPUs hand-shake through the flags (each wait
- *                             bounded at 5 s; on expiry QL_ETIMEOUT in the
- *                             device error word).  All GPUs make the same
- *                             sequence of calls.  The result, at
- *                             ql_peer_exchange_output(), is complete for work
- *                             enqueued after the call on the same stream and
- *                             valid until this GPU's next call.  The kernels'
- *                             arguments do not change between calls, so the
- *                             call can be captured in a CUDA graph. */
+ *                             bounded by the peer wait limit, 5 s unless set
+ *                             by ql_set_wait_limits; on expiry QL_ETIMEOUT in
+ *                             the device error word, which the caller checks
+ *                             with ql_device_error after synchronising).  All
+ *                             GPUs make the same sequence of calls.  The
+ *                             result, at ql_peer_exchange_output(), is
+ *                             complete for work enqueued after the call on the
+ *                             same stream and valid until this GPU's next
+ *                             call.  The kernels' arguments do not change
+ *                             between calls, so the call can be captured in a
+ *                             CUDA graph. */
 #define QL_IPC_HANDLE_BYTES 64
 int ql_peer_exchange_create(size_t bytes, void* ipc_handle, void** exchange);
 int ql_peer_exchange_connect(void* exchange, int rank, int world, const void* handles);
@@ -213,10 +232,10 @@ int ql_peer_exchange_destroy(void* exchange);
 /* ql_matmul_dev without any device allocation (no counterpart in the
  * reference, which allocates its activation scratch on every call,
  * kernel/quantized_matmul.cpp:532-534).  For callers that cannot allocate
- * device memory when they run a layer: code being captured into a CUDA graph
- * (cudaMalloc is not allowed during capture), serving runtimes whose allocator
- * owns all of HBM, and per-token loops that cannot pay for an allocation or the
- * synchronisation a free implies.  The quantized activations live in a fixed
+ * device memory when they run a layer: serving runtimes whose allocator owns
+ * all of HBM (weights and KV cache are reserved up front and nothing else may
+ * call cudaMalloc), and per-token loops that cannot pay for an allocation or
+ * the device-wide synchronisation a free implies.  The quantized activations live in a fixed
  * QL_NOALLOC_SCRATCH_BYTES array compiled into the library, held by every GPU
  * that loads it until exit; requests that need more (ql_workspace_bytes(handle,
  * M) larger than that) return QL_ESCRATCH.  The first call on a device looks up

@@ -38,13 +38,26 @@ def _p(a):
     return a.ctypes.data_as(_vp) if a is not None else None
 
 
+def reference_checkout(reference=None):
+    """The reference checkout to compile ``_ref`` from: ``reference``, else the
+    ``BREEZE_REFERENCE`` environment variable, else a directory named
+    ``reference`` beside this repository; None when none of them holds
+    ``kernel/quantized_matmul.cpp`` (e.g. on a GPU box, which uses the
+    prebuilt ``_ref`` files)."""
+    for ref in (reference, os.environ.get("BREEZE_REFERENCE"),
+                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")):
+        if ref and os.path.isfile(os.path.join(ref, "kernel", "quantized_matmul.cpp")):
+            return ref
+    return None
+
+
 def build(reference=None):
     """Build ``liboracle.so`` (and ``_ref`` when the reference checkout exists)."""
     targets = ["oracle"]
-    ref = reference or "/root/reference"
-    if os.path.isfile(os.path.join(ref, "kernel", "quantized_matmul.cpp")):
+    ref = reference_checkout(reference)
+    if ref:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={ref}", *targets], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={ref or ''}", *targets], check=True)
 
 
 def weight_scales_f32(scales):

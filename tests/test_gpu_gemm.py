@@ -138,17 +138,27 @@ def test_gemm_quantize_once_matches_matmul():
         qlc.free(h)
 
 
-@pytest.mark.slow
-def test_gemm_prefill_full_size_sampled_columns(oracle):
-    """The prefill configuration (K = 5120, N = 17408, INT4, 512 tokens): a random
-    sample of 16-column groups matches the oracle bit for bit (each column slice
-    of the MatMulNBits arrays is an exact sub-problem)."""
+@pytest.fixture(scope="module")
+def prefill_weights():
+    """configs[2]'s layer (K = 5120, N = 17408): N(0, 0.02) weights RTN-packed
+    to INT4 with zero points, built once for the module."""
     from breeze_engine_b200.quant import quantize_matmul_nbits
-    K, N, M = 5120, 17408, 512
-    rng = np.random.default_rng(K + N + M)
+    K, N = 5120, 17408
+    rng = np.random.default_rng(K + N)
     w = rng.normal(0, 0.02, (K, N)).astype(np.float32)
-    qw, sc, qz = quantize_matmul_nbits(w, bits=4, symmetric=False)
-    del w
+    return quantize_matmul_nbits(w, bits=4, symmetric=False)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("M", [128, 512, 2048])
+def test_gemm_prefill_full_size_sampled_columns(M, prefill_weights, oracle):
+    """The prefill configuration (K = 5120, N = 17408, INT4, M in {128, 512,
+    2048} tokens with 1% outlier channels): a random sample of 16-column groups
+    matches the oracle bit for bit (each column slice of the MatMulNBits arrays
+    is an exact sub-problem)."""
+    K, N = 5120, 17408
+    qw, sc, qz = prefill_weights
+    rng = np.random.default_rng(K + N + M)
     a = outlier_activations(M, K, 3)
     h = qlc.prepack(qw, sc, qz, N, K, 4)
     qlc.set_hi_prec(True)

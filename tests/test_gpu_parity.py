@@ -208,7 +208,7 @@ def test_device_api_rejects_bad_calls():
 
 @pytest.mark.slow
 def test_config1_full_size_bit_exact(oracle):
-    """BASELINE config 1 (INT4, M=1, K=N=4096) against the oracle on every output."""
+    """The benchmark spec's first config (INT4, M=1, K=N=4096) against the oracle on every output."""
     from breeze_engine_b200.quant import quantize_matmul_nbits
     rng = np.random.default_rng(0)
     w = rng.normal(0, 0.02, (4096, 4096)).astype(np.float32)
@@ -225,7 +225,7 @@ def test_config1_full_size_bit_exact(oracle):
 @pytest.mark.slow
 @pytest.mark.parametrize("K,N,bits,M", [(4096, 151936, 8, 16), (12288, 4096, 8, 16), (5120, 17408, 4, 64)])
 def test_full_size_sampled_columns(K, N, bits, M, oracle):
-    """Full BASELINE shapes: every output column of a random sample matches the
+    """Full benchmark-spec shapes: every output column of a random sample matches the
     oracle bit for bit (outputs are independent per column, so a column slice of
     the MatMulNBits arrays is an exact sub-problem)."""
     from breeze_engine_b200.quant import quantize_matmul_nbits

@@ -1,14 +1,16 @@
 """ql_matmul_dev_noalloc: the entry point for callers that cannot allocate
-device memory when they run a layer (inside CUDA-graph capture, under a
-serving runtime whose allocator owns all of HBM, or in a per-token loop that
-cannot pay for an allocation).  It keeps the quantized activations in a fixed
-scratch array compiled into the library instead of a caller or library
+device memory when they run a layer (under a serving runtime whose allocator
+owns all of HBM, or in a per-token loop that cannot pay for an allocation or
+the synchronisation a free implies).  It keeps the quantized activations in a
+fixed scratch array compiled into the library instead of a caller or library
 workspace.
 
 The test drives it through the C ABI and compares it with the workspace entry
-point (ql_matmul_dev_ws) on two calls in a row; outputs must be bit-identical,
-the same bar as every other parity test here.  The file is named so pytest
-collects it last, and it needs no state from earlier tests.
+point (ql_matmul_dev_ws) and with the oracle on calls in a row, over the
+decode kernel (M <= 64) and the tensor-core GEMM (M > 64, which also fits the
+scratch at K = 4096); outputs must be bit-identical, the same bar as every
+other parity test here.  The file is named so pytest collects it last, and it
+needs no state from earlier tests.
 """
 import ctypes
 
@@ -34,7 +36,7 @@ def _noalloc(h, a, N):
     return rc, dC.cpu().numpy()
 
 
-def test_noalloc_matches_workspace_entry_point_on_two_calls():
+def test_noalloc_matches_workspace_entry_point_on_two_calls(oracle):
     from breeze_engine_b200.quant import quantize_matmul_nbits
     rng = np.random.default_rng(42)
     K, N = 4096, 1024
@@ -43,12 +45,15 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
     h = qlc.prepack(qw, sc, qz, N, K, 4)
     qlc.set_hi_prec(True)
     try:
-        # two calls in a row: the second reuses the scratch the first left behind
-        for M in (16, 3):
+        # calls in a row: each reuses the scratch the previous one left behind;
+        # 128 tokens take the tensor-core GEMM, whose records also fit
+        for M in (16, 3, 128, 128):
+            assert qlc.lib().ql_workspace_bytes(_vp(h), M) <= 8 << 20
             a = rng.standard_normal((M, K)).astype(np.float32)
             rc, got = _noalloc(h, a, N)
             assert rc == 0, qlc.lib().ql_error_string(rc)
             assert bits_equal(got, qlc.matmul_dev(h, a, N))
+            assert bits_equal(got, oracle.matmul(qw, sc, qz, N, K, 4, a))
         assert qlc.device_error() == 0
     finally:
         qlc.free(h)
