@@ -28,6 +28,7 @@ SIGNATURES = [
     ("i4_prepack", _vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     ("i4_free", None, [_vp]),
     ("i4_matmul", None, [_vp, _vp, _i, _vp]),
+    ("i4_matmul_region", None, [_vp, _vp, _i, _vp, _vp, _vp]),
     ("ql_version", _i, []),
     ("ql_device_count", _i, []),
     ("ql_get_hi_prec", _i, []),

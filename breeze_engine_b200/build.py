@@ -39,11 +39,11 @@ def build(force=False, debug=False, verbose=False):
         return LIB
     tmp = LIB + f".{os.getpid()}.tmp"
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
+           "-Xcompiler", "-fvisibility=hidden", "-Xcompiler", "-fopenmp", "--expt-relaxed-constexpr",
            "-I", os.path.join(os.path.dirname(HERE), "include"),
            *([] if not debug else ["-DQL_DEBUG"]),
            *([] if not verbose else ["-Xptxas", "-v"]),
-           *[os.path.join(CSRC, s) for s in SOURCES], "-o", tmp]
+           *[os.path.join(CSRC, s) for s in SOURCES], "-lgomp", "-o", tmp]
     try:
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIB)

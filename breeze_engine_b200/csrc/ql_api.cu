@@ -967,3 +967,20 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
     if (e == cudaSuccess) take_device_error(st, err_word, s);
     else cuda_status(e);
 }
+
+// i4_matmul_region (kernel/quantized_matmul.cpp:554-572): called by EVERY
+// thread of the caller's OpenMP parallel region (the reference's Phi decoder
+// keeps one region open for its whole forward, kernel/phi35_decoder.cpp:179-211).
+// One thread makes the synchronous i4_matmul call and the single construct's
+// barrier holds the others until the output is complete, as the reference's
+// closing barrier does.  au8/ascale are the caller's CPU quantization scratch
+// in the reference; the GPU path quantizes into device memory and leaves them
+// untouched.  Called outside a parallel region it is i4_matmul.  Unlike the
+// reference there is no M <= 8 limit.  The status is that of the thread that
+// ran the call.
+QL_API void i4_matmul_region(void* handle, const float* A, int M, float* C, uint8_t* au8, float* ascale) {
+    (void)au8;
+    (void)ascale;
+#pragma omp single
+    i4_matmul(handle, A, M, C);
+}

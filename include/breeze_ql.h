@@ -87,6 +87,15 @@ void i4_free(void* handle);
  * ql_last_status(). */
 void i4_matmul(void* handle, const float* A, int M, float* C);
 
+/* Replaces i4_matmul_region (kernel/quantized_matmul.cpp:554-572): the same
+ * product, called by every thread of the caller's OpenMP parallel region (the
+ * Phi decoder's persistent region, kernel/phi35_decoder.cpp:179-211).  One
+ * thread issues the synchronous GPU call; the others wait at the barrier that
+ * ends it, so C is complete in every thread on return.  au8 (2*M*K bytes) and
+ * ascale (M*K/32 floats) are the reference's CPU quantization scratch: accepted
+ * and left untouched.  Outside a parallel region it behaves as i4_matmul. */
+void i4_matmul_region(void* handle, const float* A, int M, float* C, uint8_t* au8, float* ascale);
+
 /* ---------------------------------------------------------------- group 2 */
 
 /* Library ABI version (no counterpart in the reference). */

@@ -57,6 +57,8 @@ def build(reference=None):
     ref = reference_checkout(reference)
     if ref:
         targets.append("ref")
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "breeze_engine_b200", "libbreeze_ql.so")):
+            targets.append("decoders")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={ref or ''}", *targets], check=True)
 
 
