@@ -364,7 +364,7 @@ class PrefillWorkload:
     metric = "prefill GEMM INT8 TOPS (INT4 weights, two-pass INT16 activations; 4*M*N*K per call)"
     unit = "TOPS"
     K, N, Ms, bits = 5120, 17408, [128, 512, 2048], 4
-    kernel = "gemm16_kernel (ql_gemm16.cu, tcgen05 kind::f16)"
+    kernel = "gemmw_kernel (ql_gemmw.cu, tcgen05 kind::f16 on per-call FP16-dequantized weights)"
 
     def build(self, lib, world, rank):
         layer = Layer(lib, self.K, self.N, self.bits, world, rank, 3000, len(self.Ms))
@@ -388,7 +388,7 @@ class PrefillWorkload:
         return prefill_ops(M, K, n_local)
 
     def roofline(self, achieved, kern_amount_avg, calls, clock_mhz):
-        # INT4 weights with fp16 scales in two-pass mode run gemm16_kernel: per
+        # INT4 weights with fp16 scales in two-pass mode run gemmw_kernel: per
         # 32-wide block one K = 64 FP16 MMA (h and l/256 planes) = exactly the
         # 4*M*N*K operations counted here, on the FP16 tensor pipe.  Its roofline
         # is the measured dense 16-bit tensor peak; the INT8 peak (the metric
@@ -433,7 +433,7 @@ class _OpsOrBytes:
     def __init__(self):
         self.unit = "GB/s" if self.M <= 64 else "TOPS"
         self.kernel = ("decode_kernel (ql_gemv.cu)" if self.M <= 64
-                       else "gemm16_kernel (ql_gemm16.cu, tcgen05 kind::f16)")
+                       else "gemmw_kernel (ql_gemmw.cu, tcgen05 kind::f16 on per-call FP16-dequantized weights)")
 
     def step_amount(self, calls):
         if self.unit == "GB/s":
@@ -942,12 +942,32 @@ def _measure(args, wl, lib, rank, local_rank, world):
         gk = None
         if mine(layer, M):
             c, ws = outs[(id(layer), M)], qws[(id(layer), M)]
+            # INT4 prefill takes the FP16-operand GEMM: prepare one workspace per
+            # weight copy with a full call, then time the GEMM kernel alone on them
+            prep = []
+            if M > 64 and lib.ql_workspace_bytes(ctypes.c_void_p(h0), M) > lib.ql_act_workspace_bytes(M, layer.k_local):
+                a = local_a[(id(layer), M)]
+                for h in layer.handles:
+                    n = lib.ql_workspace_bytes(ctypes.c_void_p(h), M)
+                    w = torch.empty(n, dtype=torch.uint8, device="cuda")
+                    assert lib.ql_matmul_dev_ws(ctypes.c_void_p(h), a.data_ptr(), M, c.data_ptr(), w.data_ptr(), n,
+                                                stream.cuda_stream) == 0
+                    prep.append((h, w, n))
+                torch.cuda.synchronize()
+                if lib.ql_prefill_gemm_dev(ctypes.c_void_p(prep[0][0]), prep[0][1].data_ptr(), prep[0][2], M, 1,
+                                           c.data_ptr(), stream.cuda_stream) != 0:
+                    prep = []
             gk = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gk):
                 s_ptr = torch.cuda.current_stream().cuda_stream
                 for r in range(REPS):
-                    h = layer.handles[(layer.handles.index(h0) + r) % len(layer.handles)]
-                    rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s_ptr)
+                    if prep:
+                        h, w, n = prep[(layer.handles.index(h0) + r) % len(prep)]
+                        rc = lib.ql_prefill_gemm_dev(ctypes.c_void_p(h), w.data_ptr(), n, M, 1, c.data_ptr(), s_ptr)
+                    else:
+                        h = layer.handles[(layer.handles.index(h0) + r) % len(layer.handles)]
+                        rc = lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(),
+                                                         s_ptr)
                     assert rc == 0
             gk.replay()
         nrep = max(2, args.steps // 2)
@@ -958,6 +978,7 @@ def _measure(args, wl, lib, rank, local_rank, world):
         per_call.append({"M": M, "K": layer.k_local, "N": layer.n_local, "us": round(dt * 1e6, 2),
                          wl.unit: round(wl.value(amt, dt), 1)})
         del gk
+        prep = []
     achieved = wl.value(kern_amount, kern_t)
     roofline = wl.roofline(achieved, kern_amount / len(calls), calls, clock_info.get("sm_mhz"))
     roofline["kernel"] = wl.kernel
@@ -1272,9 +1293,22 @@ def run_ncu_case(K, N, bits, M, launches=4):
     c = torch.empty((M, N), dtype=torch.float32, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
     assert lib.ql_quantize_act_dev(a.data_ptr(), M, K, 1, ws.data_ptr(), n, s) == 0
-    for i in range(launches):
-        h = layer.handles[i % len(layer.handles)]
-        assert lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s) == 0
+    full = lib.ql_workspace_bytes(ctypes.c_void_p(layer.handles[0]), M)
+    if M > 64 and full > n:
+        # INT4 prefill: full calls prepare one FP16-operand workspace per copy,
+        # then the GEMM kernel alone (ql_prefill_gemm_dev) runs `launches` times
+        prep = []
+        for h in layer.handles:
+            w = torch.empty(full, dtype=torch.uint8, device="cuda")
+            assert lib.ql_matmul_dev_ws(ctypes.c_void_p(h), a.data_ptr(), M, c.data_ptr(), w.data_ptr(), full, s) == 0
+            prep.append((h, w))
+        for i in range(launches):
+            h, w = prep[i % len(prep)]
+            assert lib.ql_prefill_gemm_dev(ctypes.c_void_p(h), w.data_ptr(), full, M, 1, c.data_ptr(), s) == 0
+    else:
+        for i in range(launches):
+            h = layer.handles[i % len(layer.handles)]
+            assert lib.ql_matmul_quantized_dev(ctypes.c_void_p(h), ws.data_ptr(), M, 1, c.data_ptr(), s) == 0
     torch.cuda.synchronize()
     layer.free()
     print(json.dumps({"ncu_case": [K, N, bits, M], "launches": launches, "copies": copies,

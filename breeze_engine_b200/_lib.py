@@ -61,6 +61,7 @@ SIGNATURES = [
     ("ql_weight_serialize", _i, [_vp, _vp, _sz]),
     ("ql_weight_deserialize", _i, [_vp, _sz, ctypes.POINTER(_vp)]),
     ("ql_block_sums_dev", _i, [_vp, _vp, _i, _vp, _vp]),
+    ("ql_prefill_gemm_dev", _i, [_vp, _vp, _sz, _i, _i, _vp, _vp]),
     ("ql_quantize_dev", _i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
 ]
 

@@ -158,6 +158,31 @@ size_t ws_bytes_for(int M, int nblk) {
     return chunks * chunk_bytes(M, nblk);
 }
 
+// The INT4 FP16-operand prefill (ql_gemmw.cu) runs when the selector is
+// automatic and the weight qualifies (INT4, fp16 scales); its workspace holds
+// the FP16 activation records (sized for two-pass, the larger) and then the
+// call's dequantized weights.
+bool gemmw_applies(const Weight* w, int M) {
+    return use_gemm(M) && gemmw_supports(w) && prefill_kernel() == QL_PREFILL_AUTO;
+}
+size_t gemmw_act_region(int M, int nblk) { return align256(gemmw_act_bytes(M, nblk, true)); }
+size_t gemmw_ws_bytes(const Weight* w, int M) {
+    return gemmw_act_region(M, w->nblk) + gemmw_weight_bytes(w);
+}
+// The workspace one call on `w` asks for (ql_workspace_bytes): the FP16-operand
+// path's where it applies, else the quantized-activation records.
+size_t ws_bytes_for_w(const Weight* w, int M) {
+    const size_t base = ws_bytes_for(M, w->nblk);
+    return gemmw_applies(w, M) ? std::max(base, gemmw_ws_bytes(w, M)) : base;
+}
+
+// Dequantize the weights and quantize A into the FP16-operand workspace.
+int run_gemmw_prep(const Weight* w, const float* dA, int M, uint8_t* ws, cudaStream_t stream, bool hi_prec) {
+    cudaError_t e = launch_dequant_w16(w, hi_prec, ws + gemmw_act_region(M, w->nblk), stream);
+    if (e == cudaSuccess) e = launch_quantize_f16(dA, w->K, M, w->K, hi_prec, ws, stream);
+    return cuda_status(e);
+}
+
 ActView chunk_view(void* ws, int M, int nblk, int c, bool hi_prec) {
     const int m0 = c * MAX_DECODE_TOKENS;
     const int mc = std::min(MAX_DECODE_TOKENS, M - m0);
@@ -199,8 +224,17 @@ int run_compute(const Weight* w, const void* ws, int M, float* dC, int32_t* dCS,
 // before it reads activations or writes anything.
 int run_matmul(const Weight* w, const float* dA, int M, float* dC, int32_t* dCS, void* ws,
                size_t ws_bytes, cudaStream_t stream, bool hi_prec) {
-    if (ws_bytes < ws_bytes_for(M, w->nblk) || reinterpret_cast<uintptr_t>(ws) % 16)
-        return set_status(QL_EINVAL);        // bulk copies read the workspace in 16-byte units
+    if (reinterpret_cast<uintptr_t>(ws) % 16) return set_status(QL_EINVAL);   // 16-byte bulk copies
+    if (gemmw_applies(w, M) && ws_bytes >= gemmw_ws_bytes(w, M)) {
+        // INT4 prefill with room for the FP16 operands: dequantize once, then
+        // the FP16-operand GEMM (a smaller workspace runs the streaming GEMM)
+        uint8_t* base = static_cast<uint8_t*>(ws);
+        int rc = run_gemmw_prep(w, dA, M, base, stream, hi_prec);
+        if (rc != QL_OK) return rc;
+        return cuda_status(launch_gemmw(w, base + gemmw_act_region(M, w->nblk), base, M, hi_prec, dC, w->N, dCS,
+                                        stream));
+    }
+    if (ws_bytes < ws_bytes_for(M, w->nblk)) return set_status(QL_EINVAL);
     int rc = run_quantize(dA, M, w->K, ws, stream, hi_prec);
     if (rc != QL_OK) return rc;
     return run_compute(w, ws, M, dC, dCS, stream, hi_prec, /*pdl=*/true);
@@ -269,7 +303,8 @@ int prefill_kernel() { return g_prefill_kernel.load(std::memory_order_relaxed); 
 }  // namespace ql
 
 QL_API int ql_set_prefill_kernel(int kind) {
-    if (kind != ql::QL_PREFILL_AUTO && kind != ql::QL_PREFILL_I8 && kind != ql::QL_PREFILL_F16_PAIR)
+    if (kind != ql::QL_PREFILL_AUTO && kind != ql::QL_PREFILL_I8 && kind != ql::QL_PREFILL_F16_PAIR &&
+        kind != ql::QL_PREFILL_F16_STREAM)
         return set_status(QL_EINVAL);
     g_prefill_kernel.store(kind, std::memory_order_relaxed);
     return set_status(QL_OK);
@@ -575,7 +610,7 @@ QL_API int ql_weight_deserialize(const void* host_buf, size_t bytes, void** out_
 QL_API size_t ql_workspace_bytes(const void* handle, int M) {
     if (!valid_weight(handle) || M <= 0) return 0;
     const auto* w = static_cast<const Weight*>(handle);
-    return ws_bytes_for(M, w->nblk);
+    return ws_bytes_for_w(w, M);
 }
 
 static int check_call(const void* handle, const float* dA, int M, const void* dOut) {
@@ -609,7 +644,7 @@ QL_API int ql_matmul_dev(void* handle, const float* dA, int M, float* dC, void* 
     const bool hp = ql_get_hi_prec() != 0;
     std::lock_guard<std::mutex> lk(g_mu);
     DeviceState* st = state_for(w->device);
-    const size_t need = ws_bytes_for(M, w->nblk);
+    const size_t need = ws_bytes_for_w(w, M);
     cudaError_t e = ensure(&st->ws, &st->ws_bytes, need);
     if (e != cudaSuccess) return cuda_status(e);
     return run_matmul(w, dA, M, dC, nullptr, st->ws, st->ws_bytes, static_cast<cudaStream_t>(stream), hp);
@@ -831,7 +866,7 @@ QL_API int ql_block_sums_dev(void* handle, const float* dA, int M, int32_t* dCS,
     const bool hp = ql_get_hi_prec() != 0;
     std::lock_guard<std::mutex> lk(g_mu);
     DeviceState* st = state_for(w->device);
-    cudaError_t e = ensure(&st->ws, &st->ws_bytes, ws_bytes_for(M, w->nblk));
+    cudaError_t e = ensure(&st->ws, &st->ws_bytes, ws_bytes_for_w(w, M));
     if (e != cudaSuccess) return cuda_status(e);
     return run_matmul(w, dA, M, nullptr, dCS, st->ws, st->ws_bytes, static_cast<cudaStream_t>(stream), hp);
 }
@@ -893,7 +928,7 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
     cudaStream_t s = internal_stream(st);
     const size_t a_bytes = align256(static_cast<size_t>(M) * w->K * 4);
     const size_t c_bytes = align256(static_cast<size_t>(M) * w->N * 4);
-    const size_t ws_bytes = ws_bytes_for(M, w->nblk);
+    const size_t ws_bytes = ws_bytes_for_w(w, M);
     cudaError_t e = ensure(&st->buf, &st->buf_bytes, a_bytes + c_bytes + ws_bytes);
     if (e != cudaSuccess) {
         cuda_status(e);
@@ -938,7 +973,9 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
             return;
         }
     }
-    int rc = run_quantize(dA, M, w->K, ws, s, hp);
+    const bool fp16_ops = gemmw_applies(w, M);      // the workspace was sized for it above
+    uint8_t* wbase = static_cast<uint8_t*>(ws);
+    int rc = fp16_ops ? run_gemmw_prep(w, dA, M, wbase, s, hp) : run_quantize(dA, M, w->K, ws, s, hp);
     if (rc != QL_OK) return;
     // column chunks of whole 128-column tiles; the last takes the remainder
     const int per = ((w->N / chunks) / 128) * 128;
@@ -949,7 +986,12 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
         view.N = nc;
         view.G = nc / 16;
         view.W = w->W + static_cast<size_t>(n0 / 16) * w->nblk * w->REC;
-        rc = run_compute(&view, ws, M, dC + n0, nullptr, s, hp, /*pdl=*/i == 0, /*ldc=*/w->N);
+        if (fp16_ops) {
+            const uint8_t* wd = wbase + gemmw_act_region(M, w->nblk) + static_cast<size_t>(n0 / 128) * w->nblk * WREC16;
+            rc = cuda_status(launch_gemmw(&view, wd, wbase, M, hp, dC + n0, w->N, nullptr, s));
+        } else {
+            rc = run_compute(&view, ws, M, dC + n0, nullptr, s, hp, /*pdl=*/i == 0, /*ldc=*/w->N);
+        }
         if (rc != QL_OK) break;
         e = cudaEventRecord(st->chunk_done[i], s);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st->copy_stream, st->chunk_done[i], 0);
@@ -983,4 +1025,24 @@ QL_API void i4_matmul_region(void* handle, const float* A, int M, float* C, uint
     (void)ascale;
 #pragma omp single
     i4_matmul(handle, A, M, C);
+}
+
+// The FP16-operand prefill GEMM alone, on a workspace a previous
+// ql_matmul_dev_ws call with the same handle, M and activation mode has just
+// filled (it still holds that call's dequantized weights and FP16 activations):
+// the kernel-only timing of a prefill call, without its dequantize and quantize
+// passes.  QL_ENOTSUP where the call would not take that path.
+QL_API int ql_prefill_gemm_dev(void* handle, const void* ws, size_t ws_bytes, int M, int hi_prec, float* dC,
+                               void* stream) {
+    if (!valid_weight(handle) || M <= 0 || !ws || !dC || reinterpret_cast<uintptr_t>(ws) % 16)
+        return set_status(QL_EINVAL);
+    const auto* w = static_cast<const Weight*>(handle);
+    if (!gemmw_applies(w, M)) return set_status(QL_ENOTSUP);
+    if (ws_bytes < gemmw_ws_bytes(w, M)) return set_status(QL_EINVAL);
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return set_status(QL_ECUDA);
+    if (dev != w->device) return set_status(QL_EDEVICE);
+    const uint8_t* base = static_cast<const uint8_t*>(ws);
+    return cuda_status(launch_gemmw(w, base + gemmw_act_region(M, w->nblk), base, M, hi_prec != 0, dC, w->N,
+                                    nullptr, static_cast<cudaStream_t>(stream)));
 }

@@ -58,7 +58,10 @@ __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
-// The wait limits in force (read once per wait that did not succeed at once).
+// The wait limits in force.  Waits read them only once they have lasted
+// WAIT_CHECK_NS (a global load, kept off the fast path of the pipelines'
+// waits, which usually end within microseconds), so limits below 1 ms act as 1 ms.
+constexpr unsigned long long WAIT_CHECK_NS = 1000000ull;
 __device__ __forceinline__ uint64_t wait_limit(const int* err) {
     return err ? *reinterpret_cast<const volatile unsigned long long*>(&reinterpret_cast<const DeviceCtl*>(err)->wait_ns)
                : WAIT_LIMIT_NS;
@@ -134,10 +137,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    const uint64_t limit = wait_limit(err);
+    uint64_t limit = WAIT_CHECK_NS;
+    bool read = false;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > limit) break;
+        if (global_ns() - t0 > limit) {
+            if (read) break;
+            limit = wait_limit(err);
+            read = true;
+        }
     }
     record_error(err, QL_ETIMEOUT);
     return false;

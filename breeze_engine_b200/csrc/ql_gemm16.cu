@@ -584,10 +584,16 @@ __device__ __forceinline__ bool pair_wait(uint32_t bar, uint32_t parity, int* er
     bool ok = mbar_try_wait_cluster(bar, parity, 0);
     if (!ok) {
         const uint64_t t0 = global_ns();
-        const uint64_t limit = wait_limit(err);
+        uint64_t limit = WAIT_CHECK_NS;     // the device limit is read once this much has passed
+        bool read = false;
         while (true) {
             if (mbar_try_wait_cluster(bar, parity, 10000)) { ok = true; break; }
             if (*abort_flag) break;
+            if (global_ns() - t0 > limit && !read) {
+                limit = wait_limit(err);
+                read = true;
+                continue;
+            }
             if (global_ns() - t0 > limit) {
                 record_error(err, QL_ETIMEOUT);
                 *abort_flag = 1;

@@ -123,8 +123,26 @@ cudaError_t launch_gemm(const Weight* w, const uint8_t* act, int M, bool hi_prec
 bool gemm16_supports(const Weight* w, bool hi_prec);
 cudaError_t launch_gemm16(const Weight* w, const uint8_t* act, int M, float* C, int ldc, int32_t* cs,
                           cudaStream_t stream);
-enum : int { QL_PREFILL_AUTO = 0, QL_PREFILL_I8 = 1, QL_PREFILL_F16_PAIR = 2 };
+enum : int { QL_PREFILL_AUTO = 0, QL_PREFILL_I8 = 1, QL_PREFILL_F16_PAIR = 2, QL_PREFILL_F16_STREAM = 3 };
 int prefill_kernel();                                    // ql_api.cu
+
+// INT4 prefill on pre-expanded FP16 operands (ql_gemmw.cu): the one-call
+// entry points, given a workspace of ws_bytes_for_w() bytes, dequantize the
+// weights once per call into [n_tiles][nblk][WREC16] (128 rows x 32 k FP16
+// q - zp in the canonical tcgen05 A layout, then 128 fp32 weight scales) and
+// quantize the activations into [m_tiles][nblk][AREC16_HP or _SP] (FP16 h and
+// l/256 planes, or q8, in the B layout, then 128 fp32 activation scales).
+constexpr int WREC16 = 128 * 32 * 2 + 128 * 4;           // 8704
+constexpr int AREC16_HP = 2 * 128 * 32 * 2 + 128 * 4;    // 16896
+constexpr int AREC16_SP = 128 * 32 * 2 + 128 * 4;        // 8704
+bool gemmw_supports(const Weight* w);
+size_t gemmw_act_bytes(int M, int nblk, bool hi_prec);
+size_t gemmw_weight_bytes(const Weight* w);
+cudaError_t launch_dequant_w16(const Weight* w, bool hi_prec, uint8_t* out, cudaStream_t stream);
+cudaError_t launch_quantize_f16(const float* A, int lda, int M, int K, bool hi_prec, uint8_t* out,
+                                cudaStream_t stream, const NormArgs* norm = nullptr);
+cudaError_t launch_gemmw(const Weight* w, const uint8_t* wd, const uint8_t* ad, int M, bool hi_prec, float* C,
+                         int ldc, int32_t* cs, cudaStream_t stream);
 
 // Size of the fixed scratch behind ql_matmul_dev_noalloc (ql_api.cu); the
 // public header states the same value as QL_NOALLOC_SCRATCH_BYTES.

@@ -87,9 +87,15 @@ __device__ bool wait_flags(const uint8_t* region, int P, unsigned int e, int* er
     bool ok = true;
     if (q < P) {
         const uint64_t t0 = global_ns();
-        const uint64_t limit = peer_wait_limit(err);
+        uint64_t limit = WAIT_CHECK_NS;                // the device limit is read once this much has passed
+        bool read = false;
         while (static_cast<int>(read_flag(region, q) - e) < 0) {
             if (global_ns() - t0 > limit) {
+                if (!read) {
+                    limit = peer_wait_limit(err);
+                    read = true;
+                    continue;
+                }
                 record_error(err, QL_ETIMEOUT);
                 ok = false;
                 break;

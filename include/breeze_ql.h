@@ -109,12 +109,15 @@ int ql_device_count(void);
 int ql_get_hi_prec(void);
 
 /* Prefill kernel selector (no counterpart in the reference, whose i4_matmul
- * has one CPU path): 0 = automatic -- M > 64 tokens with INT4 weights, fp16
- * scales and two-pass activations run the tcgen05 kind::f16 GEMM, every other
- * prefill the kind::i8 GEMM; 1 = always the kind::i8 GEMM; 2 = the kind::f16
- * GEMM on CTA pairs (cta_group::2) where it applies.  All kernels give the
- * reference's bits; the switch exists for comparison and testing.
- * Process-global; returns QL_EINVAL for any other value. */
+ * has one CPU path): 0 = automatic -- M > 64 tokens with INT4 weights and
+ * fp16 scales run the FP16-operand tcgen05 GEMM (the weights dequantized once
+ * per call into the workspace, ql_workspace_bytes) when the call has that
+ * workspace, else the kind::f16 GEMM that unpacks them per tile (two-pass);
+ * every other prefill the kind::i8 GEMM; 1 = always the kind::i8 GEMM; 2 =
+ * the per-tile-unpack kind::f16 GEMM on CTA pairs (cta_group::2) where it
+ * applies; 3 = that GEMM on single CTAs.  All kernels give the reference's
+ * bits; the switch exists for comparison and testing.  Process-global;
+ * returns QL_EINVAL for any other value. */
 int ql_set_prefill_kernel(int kind);
 
 /* Status of this thread's last call, and its description. */
@@ -151,7 +154,9 @@ int ql_weight_info(const void* handle, int* N, int* K, int* bits, int* device,
 
 /* Scratch bytes ql_matmul_dev_ws needs for M rows (quantized activations;
  * M > 64 uses the tensor-core GEMM's record layout, so the size is not linear
- * in M across that boundary). */
+ * in M across that boundary; for INT4 weights with fp16 scales it also holds
+ * the call's FP16-dequantized weights, 2.125 bytes per weight -- a smaller
+ * workspace of at least the activation records runs the per-tile-unpack GEMM). */
 size_t ql_workspace_bytes(const void* handle, int M);
 
 /* Device twin of i4_matmul (kernel/quantized_matmul.cpp:528): dA [M,K] fp32
@@ -252,6 +257,15 @@ int ql_peer_exchange_destroy(void* exchange);
  * share the array: calls whose work overlaps on the GPU race, so serialise them.
  * Same numerics and arguments as ql_matmul_dev. */
 int ql_matmul_dev_noalloc(void* handle, const float* dA, int M, float* dC, void* stream);
+
+/* The FP16-operand prefill GEMM alone (no counterpart in the reference): re-runs
+ * the tensor-core GEMM of the last ql_matmul_dev_ws call made with the same
+ * handle, M (> 64), activation mode and workspace, on the dequantized weights
+ * and FP16 activations that call left in the workspace -- the kernel-only
+ * timing of a prefill call.  QL_ENOTSUP where that call does not take the
+ * FP16-operand path (not INT4 with fp16 scales, or a selector other than 0). */
+int ql_prefill_gemm_dev(void* handle, const void* ws, size_t ws_bytes, int M, int hi_prec, float* dC,
+                        void* stream);
 
 /* Packed-layout cache (no counterpart in the reference, which repacks every
  * MatMulNBits weight on each load, breeze/qwen35_cpu.py:71-89 ->
