@@ -36,17 +36,30 @@
 // tile fastest (concurrent CTAs share a weight tile through L2).  Warps:
 //   0     producer: per stage of BPS blocks one bulk copy of the weight records
 //         and one of the activation records (no multicast)
-//   1     MMA: TMEM owner; lane 0 issues per block 4 (two-pass) or 2 MMAs of
-//         128x128x16 into one of 4 accumulator slots of 128 columns
-//   2     scales: copies each block's 1 KB of scales from the stage into the
+//   1-2   MMA: two issuing warps take alternate stages; lane 0 issues per block
+//         4 (two-pass) or 2 MMAs of 128x128x16 into one of 4 accumulator slots
+//         of 128 columns (warp 1 owns the TMEM allocation).  Measured on B200:
+//         an mbarrier wait (even on a completed phase) or a shared-memory
+//         access in the issuing warp does not proceed until that warp's queued
+//         MMAs have finished, so one issuer that waits once per block (the
+//         per-block hand-off to the epilogue is the reference's per-block
+//         rescale) drains the tensor pipe every block: 506 cycles per block
+//         instead of 273.  With two issuers, each drains only its own previous
+//         stage while the other's MMAs run (256 cycles per block).  Each issuer
+//         does all of a stage's waits before issuing any of its MMAs.
+//   3     scales: copies each block's 1 KB of scales from the stage into the
 //         scale ring the epilogue reads, then fences its generic reads of the
-//         stage against the stage's next bulk copy.  (Done by the MMA warp,
-//         whose lane 0 has MMAs in flight, that fence held every block's MMAs
-//         until the previous block's had finished: the tensor pipe ran 20% busy.)
-//   3-10  epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 weight rows) and
-//         64 token columns per block with two 32-column loads and one wait,
-//         releases the slot, and runs the FP32 chain in registers (loading 8
-//         columns at a time, one load latency per chunk bounded the kernel).
+//         stage against the stage's next bulk copy (off the issuing warps,
+//         whose own proxy fence would stall them the same way).
+//   4-11  epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 weight rows) and
+//         64 token columns per block with two 32-column loads and one wait
+//         (no shared-memory access between a load and its wait: a warp's
+//         shared-memory accesses wait for its outstanding tcgen05.ld), releases
+//         the slot, and runs the FP32 chain in registers, reading the block's
+//         activation scales 16 columns at a time.  (Tried and slower on B200:
+//         16 epilogue warps of 32 columns -- the 96-register cap spills --
+//         and loading the next half while rescaling the current one, whose
+//         scale reads then waited for that load.)
 // Every wait is bounded (the device wait limit) and sets the device error
 // word; on a failure all roles stop, bulk copies and MMAs in flight are
 // drained (bounded) and TMEM is freed.
@@ -66,7 +79,8 @@ constexpr int W_T = 128;                     // weight rows per tile (MMA M)
 constexpr int A_T = 128;                     // tokens per tile (MMA N)
 constexpr int W_TILE = W_T * 32 * 2;         // FP16 weight tile of one block (8 KB)
 constexpr int N_EPI = 8;
-constexpr int N_WARPS = 3 + N_EPI;
+constexpr int N_WARPS = 4 + N_EPI;
+constexpr int W_SC = 3;                      // scale warp; warps 1 and 2 issue MMAs, 4.. are the epilogue
 constexpr int E_COLS = 64;                   // token columns per epilogue thread
 constexpr int N_ACC = 4;                     // TMEM accumulator slots of 128 columns
 constexpr int N_SC = 8;                      // scale ring (1 KB per block)
@@ -276,7 +290,7 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
             mbar_init(smem_u32(&sc_full[k]), 1);
             mbar_init(smem_u32(&sc_empty[k]), N_EPI);
         }
-        mbar_init(smem_u32(drain), 1);
+        mbar_init(smem_u32(drain), 2);             // one commit per issuing warp
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -321,26 +335,34 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
         const int issued = si;
         for (int k = std::max(0, issued - p.STAGES); k < issued; ++k)
             mbar_wait(smem_u32(&st_full[k % p.STAGES]), (k / p.STAGES) & 1, p.err);
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        // Warp 1 takes the even stages of the CTA's stage sequence, warp 2 the odd ones.
         constexpr uint32_t idesc = make_idesc_f16(W_T, A_T);
+        const int parity = warp - 1;
         int si = 0, bi = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
             for (int ks = 0; ks < spt && ok; ++ks, ++si) {
-                const int s = si % p.STAGES;
-                if (!(ok = warp_wait(smem_u32(&st_full[s]), (si / p.STAGES) & 1, p.err, abort_flag))) break;
-                const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
                 const int nb = min(p.BPS, p.nblk - ks * p.BPS);
-                for (int j = 0; j < nb; ++j, ++bi) {
-                    const int ac = bi % N_ACC;
-                    if (bi >= N_ACC &&
-                        !(ok = warp_wait(smem_u32(&acc_empty[ac]), ((bi / N_ACC) - 1) & 1, p.err, abort_flag)))
-                        break;
-                    tc_fence_after();
-                    if (lane == 0) {
+                const int bi0 = bi;
+                bi += nb;
+                if ((si & 1) != parity) continue;
+                const int s = si % p.STAGES;
+                // every wait of the stage before its first MMA
+                if (!(ok = warp_wait(smem_u32(&st_full[s]), (si / p.STAGES) & 1, p.err, abort_flag))) break;
+                for (int j = 0; j < nb && ok; ++j) {
+                    const int b = bi0 + j;
+                    if (b >= N_ACC)
+                        ok = warp_wait(smem_u32(&acc_empty[b % N_ACC]), ((b / N_ACC) - 1) & 1, p.err, abort_flag);
+                }
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
+                    for (int j = 0; j < nb; ++j) {
                         const uint32_t a0 = smem_u32(st + j * WREC16), b0 = smem_u32(st + w_part + j * p.arec);
-                        const uint32_t d = tmem + ac * A_T;
+                        const uint32_t d = tmem + ((bi0 + j) % N_ACC) * A_T;
                         const uint64_t da0 = make_smem_desc(a0, 2048, 128);
                         const uint64_t da1 = make_smem_desc(a0 + 4096, 2048, 128);
                         mma_f16(d, da0, make_smem_desc(b0, 2048, 128), idesc, 0);
@@ -349,18 +371,18 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
                             mma_f16(d, da0, make_smem_desc(b0 + 8192, 2048, 128), idesc, 1);
                             mma_f16(d, da1, make_smem_desc(b0 + 12288, 2048, 128), idesc, 1);
                         }
-                        mma_commit(smem_u32(&acc_full[ac]));
-                        if (j == nb - 1) mma_commit(smem_u32(&st_empty[s]));
+                        mma_commit(smem_u32(&acc_full[(bi0 + j) % N_ACC]));
                     }
-                    __syncwarp();
+                    mma_commit(smem_u32(&st_empty[s]));
                 }
+                __syncwarp();
             }
         }
-        // drain: all MMAs issued by lane 0 complete before TMEM is freed
+        // drain: all MMAs issued by this warp's lane 0 complete before TMEM is freed
         if (lane == 0) mma_commit(smem_u32(drain));
         __syncwarp();
         mbar_wait(smem_u32(drain), 0, p.err);
-    } else if (warp == 2) {
+    } else if (warp == W_SC) {
         // ------------------------------------------------------------ scales
         int si = 0, bi = 0;
         bool ok = true;
@@ -391,10 +413,11 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int e = warp - 3;
+        const int e = warp - 4;
         const int q = warp & 3;                           // TMEM lane quarter (hardware rule: warp % 4)
         const int cq = e >> 2;                            // token columns E_COLS*cq ..
         const int row = q * 32 + lane;                    // weight row within the tile
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + cq * E_COLS;
         int bi = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
@@ -409,8 +432,7 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
                 if (!(ok = warp_wait(smem_u32(&acc_full[ac]), (bi / N_ACC) & 1, p.err, abort_flag))) break;
                 tc_fence_after();
                 const float* scs = reinterpret_cast<const float*>(sc_ring + sc * SC_BYTES);
-                const float wsc = scs[row];                   // 256*bscale (two-pass) or bscale; 0 past N
-                const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ac * A_T + cq * E_COLS;
+                const uint32_t taddr = lane_base + ac * A_T;
                 if constexpr (OUT_CS) {
                     // block sums [M][N][nblk] = 256 * D (two-pass) or D (exact): a checking output
 #pragma unroll 1
@@ -433,32 +455,41 @@ __global__ void __launch_bounds__(N_WARPS * 32, 1) gemmw_kernel(const GemmWParam
                         mbar_arrive(smem_u32(&acc_empty[ac]));
                         mbar_arrive(smem_u32(&sc_empty[sc]));
                     }
-                    (void)wsc;
                 } else {
+                    const float wsc = scs[row];                   // 256*bscale (two-pass) or bscale; 0 past N
                     const uint64_t ws2 = f2_pack(wsc, wsc);
                     const float* ascale = scs + 128 + cq * E_COLS;
+                    // the whole slot in one wait (a warp's shared-memory accesses wait for
+                    // its outstanding tcgen05.ld, so the scale reads come after it)
                     uint32_t v[E_COLS];
                     tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
                     tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
                     tmem_wait_ld();
-                    // every column of the slot this warp reads is in registers: hand it back
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&acc_empty[ac]));
+                    // 16 columns at a time: their 4 scale loads issue back to back, so
+                    // one shared-memory latency covers 16 outputs
 #pragma unroll
-                    for (int k = 0; k < E_COLS; k += 4) {
-                        const float4 a4 = lds_f4(ascale + k);
-                        const uint64_t d0 = i2_pack(static_cast<int32_t>(v[k]), static_cast<int32_t>(v[k + 1]));
-                        const uint64_t d1 = i2_pack(static_cast<int32_t>(v[k + 2]), static_cast<int32_t>(v[k + 3]));
-                        acc[k >> 1] = f2_fma(f2_pack(a4.x, a4.y), f2_mul(d0, ws2), acc[k >> 1]);
-                        acc[(k >> 1) + 1] = f2_fma(f2_pack(a4.z, a4.w), f2_mul(d1, ws2), acc[(k >> 1) + 1]);
+                    for (int c0 = 0; c0 < E_COLS; c0 += 16) {
+                        float4 a4[4];
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) a4[g] = lds_f4(ascale + c0 + 4 * g);
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            const int k = c0 + 4 * g;
+                            const uint64_t d0 = i2_pack(static_cast<int32_t>(v[k]), static_cast<int32_t>(v[k + 1]));
+                            const uint64_t d1 = i2_pack(static_cast<int32_t>(v[k + 2]), static_cast<int32_t>(v[k + 3]));
+                            acc[k >> 1] = f2_fma(f2_pack(a4[g].x, a4[g].y), f2_mul(d0, ws2), acc[k >> 1]);
+                            acc[(k >> 1) + 1] = f2_fma(f2_pack(a4[g].z, a4[g].w), f2_mul(d1, ws2), acc[(k >> 1) + 1]);
+                        }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&sc_empty[sc]));
                 }
             }
             if (!ok || OUT_CS) continue;
-            // C[m, n] for this thread's 64 token columns (lanes = consecutive n)
+            // C[m, n] for this thread's token columns (lanes = consecutive n)
             if (n < p.N) {
 #pragma unroll
                 for (int i = 0; i < E_COLS / 2; ++i) {
