@@ -12,7 +12,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libbreeze_ql.so")
-SOURCES = ["ql_api.cu", "ql_quant.cu", "ql_prepack.cu", "ql_gemv.cu", "ql_gemm.cu", "ql_gemm16.cu", "ql_gemmw.cu",
+SOURCES = ["ql_api.cu", "ql_quant.cu", "ql_prepack.cu", "ql_gemv.cu", "ql_gemv4.cu", "ql_gemm.cu", "ql_gemm16.cu", "ql_gemmw.cu",
            "ql_norm.cu", "ql_peer.cu"]
 HEADERS = ["ql_common.cuh", "ql_internal.h", "ql_tcgen05.cuh", "ql_quant.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

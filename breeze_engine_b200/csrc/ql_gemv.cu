@@ -505,8 +505,9 @@ cudaError_t launch_decode(const Weight* w, const ActView& act, bool hi_prec, flo
     const int MT = act.MT;
     if (MT != 1 && MT != 2 && MT != 4 && MT != 8) return cudaErrorInvalidValue;
     if ((MT == 1 && (act.TPB < 1 || act.TPB > 8)) || (MT > 1 && act.TPB != 8 * MT) ||
-        act.TPBA < act.TPB || (act.TPBA & 3) || act.QREC != act.TPB * 4 * act.LB + act.TPBA * 4)
+        act.TPBA < act.TPB || (act.TPBA & 3) || act.QREC != act.TPB * 4 * act.LB + act.TPBA * 8)
         return cudaErrorInvalidValue;
+    if (decode_dp4a_applies(w, act)) return launch_decode_dp4a(w, act, hi_prec, C, ldc, cs, stream, pdl);
     if (cs) {
         return hi_prec ? dispatch_w<true, true>(w, p, MT, stream, pdl)
                        : dispatch_w<false, true>(w, p, MT, stream, pdl);

@@ -49,13 +49,17 @@ inline void weight_geometry(int bits, bool scale_half, bool has_zp, int* TB, int
 
 // Quantized activations in the kernels' layout (scratch produced per call):
 // one record per 32-wide K block, so a stage of blocks is one bulk copy.
-//   rec[nblk][QREC]            QREC = TPB*4*LB + TPBA*4 bytes
+//   rec[nblk][QREC]            QREC = TPB*4*LB + TPBA*8 bytes
 //     [0, TPB*4*LB)            fragments of token m at m*4*LB: slot t holds what
 //                              lane 4*(m%8)+t needs as its m16n8k32 B fragment --
 //                              two-pass (LB = 16): hi-128 (signed) of k 4t..4t+3
 //                              and 16+4t..16+4t+3, then lo (unsigned) of the same
 //                              k; single-pass (LB = 8): q8 (signed) of those k.
-//     [TPB*4*LB, QREC)         fp32 activation scales of tokens 0..TPBA-1.
+//     [TPB*4*LB, +TPBA*4)      fp32 activation scales of tokens 0..TPBA-1;
+//     [.., QREC)               int32 block sums of the quantized values (sum of
+//                              q16, or of q8), for kernels that take the zero
+//                              point out of the weights: sum q16*(q - zp) =
+//                              sum q16*q - zp * sum q16.
 // MT = token groups of 8 (1, 2, 4 or 8).  TPB = M when MT == 1 (only the real
 // tokens are stored and copied) else 8*MT; TPBA = TPB rounded up to 4.
 // Padded tokens (M..TPB-1, and scales up to TPBA) are written as zeros.
@@ -155,6 +159,11 @@ cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8
                                 float* ascale, cudaStream_t stream);
 cudaError_t launch_decode(const Weight* w, const ActView& act, bool hi_prec, float* C,
                           int ldc, int32_t* cs, cudaStream_t stream, bool pdl);
+// INT4 at one or two tokens: the dp4a decode kernel (ql_gemv4.cu), which
+// launch_decode picks where it applies.
+bool decode_dp4a_applies(const Weight* w, const ActView& act);
+cudaError_t launch_decode_dp4a(const Weight* w, const ActView& act, bool hi_prec, float* C, int ldc, int32_t* cs,
+                               cudaStream_t stream, bool pdl);
 
 cudaError_t launch_prepack_onnx(Weight* w, const uint8_t* d_qw, const void* d_scales,
                                 const uint8_t* d_qzeros, cudaStream_t stream);

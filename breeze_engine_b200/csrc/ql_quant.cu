@@ -182,7 +182,7 @@ static int act_tpba(int M) { return (act_tpb(M) + 3) & ~3; }
 
 // Sized for the two-pass layout (the larger one) whatever the mode.
 size_t act_bytes(int M, int nblk) {
-    const size_t rec = static_cast<size_t>(act_tpb(M)) * 64 + act_tpba(M) * 4;
+    const size_t rec = static_cast<size_t>(act_tpb(M)) * 64 + act_tpba(M) * 8;
     return (static_cast<size_t>(nblk) * rec + 255) & ~size_t(255);
 }
 
@@ -195,7 +195,7 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec) {
     v.nblk = nblk;
     v.hp = hi_prec ? 1 : 0;
     v.LB = hi_prec ? 16 : 8;
-    v.QREC = v.TPB * 4 * v.LB + v.TPBA * 4;
+    v.QREC = v.TPB * 4 * v.LB + v.TPBA * 8;
     v.q = static_cast<uint8_t*>(ws);
     return v;
 }

@@ -75,6 +75,7 @@ __device__ __forceinline__ void act_zero_block(const ActView& out, int m, int b)
         }
     }
     reinterpret_cast<float*>(rec + out.TPB * 4 * LB)[m] = 0.0f;
+    reinterpret_cast<int32_t*>(rec + out.TPB * 4 * LB + out.TPBA * 4)[m] = 0;
 }
 
 template <bool HP>
@@ -96,6 +97,7 @@ __device__ __forceinline__ void act_store_block(const float (&v)[32], const ActV
     scales[m] = scale;
 
     uint32_t hw[8], lw[8];
+    int qsum = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
         uint32_t hword = 0, lword = 0;
@@ -103,6 +105,7 @@ __device__ __forceinline__ void act_store_block(const float (&v)[32], const ActV
         for (int j = 0; j < 4; ++j) {
             int q = to_int_like_lrint(__fmul_rn(v[4 * w + j], inv));
             q = q > IMAX ? IMAX : (q < -IMAX ? -IMAX : q);
+            qsum += q;
             if (HP) {
                 const uint32_t u = static_cast<uint32_t>(q + 32768);
                 hword |= ((u >> 8) ^ 0x80u) << (8 * j);      // hi - 128 as a signed byte
@@ -114,6 +117,7 @@ __device__ __forceinline__ void act_store_block(const float (&v)[32], const ActV
         hw[w] = hword;
         lw[w] = lword;
     }
+    reinterpret_cast<int32_t*>(rec + out.TPB * 4 * LB + out.TPBA * 4)[m] = qsum;
     // lane t: k 4t..4t+3 (word t) and 16+4t..16+4t+3 (word 4+t) of each plane
 #pragma unroll
     for (int t = 0; t < 4; ++t) {

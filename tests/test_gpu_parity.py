@@ -304,3 +304,31 @@ def test_split_k_relay_repeatable(bits, half, N, K, M, cfg, oracle, monkeypatch)
             assert bits_equal(c.cpu().numpy(), ref)
     finally:
         qlc.free(h)
+
+
+@pytest.mark.parametrize("zp,half", [(False, True), (True, True), (True, False), (False, False)])
+@pytest.mark.parametrize("hp", [True, False])
+@pytest.mark.parametrize("K", [64, 800, 4096])
+def test_dp4a_decode_kernel(zp, half, hp, K, oracle):
+    """INT4 at one and two tokens on layers of >= 8192 rows run the dp4a
+    decode kernel (ql_gemv4.cu): outputs and per-block INT32 accumulators
+    bit-exact against the oracle, with explicit zero points, fp16/fp32 scales,
+    both activation modes, and K from 2 blocks (no K split) to 128 (split,
+    relayed accumulators).  N = 8208 leaves a partial last quad of row groups;
+    the activations include edge values (zeros, outliers)."""
+    from cases import edge_activations
+    N = 8208
+    qw, sc, qz = _weights(N, K, 4, zp, half, K + 2 * zp + half)
+    h = qlc.prepack(qw, sc, qz, N, K, 4)
+    qlc.set_hi_prec(hp)
+    try:
+        for M in (1, 2, 1):
+            a = np.random.default_rng(M + K).standard_normal((M, K)).astype(np.float32)
+            if K >= 800:
+                a[:, : K // 4] = edge_activations(M, K // 4, 3)
+            assert bits_equal(qlc.matmul_dev(h, a, N), oracle.matmul(qw, sc, qz, N, K, 4, a, hi_prec=hp)), M
+            if hp:
+                hi, lo, _ = oracle.quantize_i16(a)
+                assert np.array_equal(qlc.block_sums_dev(h, a, N, K), oracle.block_sums(qw, qz, N, K, 4, hi, lo))
+    finally:
+        qlc.free(h)
