@@ -51,6 +51,8 @@ SIGNATURES = [
     ("ql_norm_act_workspace_bytes", _sz, [_i, _i]),
     ("ql_quantize_act_rmsnorm_dev", _i, [_vp, _vp, ctypes.c_float, _i, _i, _i, _vp, _sz, _vp, _vp]),
     ("ql_matmul_rmsnorm_dev", _i, [_vp, _vp, _vp, ctypes.c_float, _i, _vp, _vp]),
+    ("ql_quantize_act_silu_mul_dev", _i, [_vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp, _vp]),
+    ("ql_matmul_silu_mul_dev", _i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
     ("ql_weight_concat", _i, [ctypes.POINTER(_vp), _i, ctypes.POINTER(_vp)]),
     ("ql_peer_exchange_create", _i, [_sz, _vp, ctypes.POINTER(_vp)]),
     ("ql_peer_exchange_connect", _i, [_vp, _i, _i, _vp]),

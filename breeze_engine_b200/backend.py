@@ -279,6 +279,44 @@ def rmsnorm_matmul(handle, x, norm_w, eps, N, out=None):
     return out
 
 
+def silu_mul_matmul(handle, gate, up, N, out=None):
+    """``matmul(silu(gate) * up)`` with the SiLU and product fused into the
+    activation quantizer: the reference decoder's ``g1 = siluf(g1) * g2``
+    followed by ``i4_matmul`` of the down projection
+    (``kernel/qwen35_decoder.cpp:408-409``), bit for bit (the host C library's
+    ``expf`` is reproduced exactly).  ``gate`` and ``up`` are fp32 CUDA tensors of
+    shape ``[M, K]`` on the handle's device whose rows share one stride (e.g. the
+    two halves of a concatenated gate|up output); asynchronous on the current
+    stream, in the process-wide activation mode (:func:`set_hi_prec`)."""
+    lib = L.load()
+    torch = _torch()
+    hN, hK, _, hdev, _ = weight_info(handle)
+    if int(N) != hN:
+        raise ValueError(f"N={N} does not match the packed weight (N={hN})")
+    if not (_is_cuda_tensor(gate) and _is_cuda_tensor(up)):
+        raise TypeError("silu_mul_matmul takes CUDA tensors")
+    if gate.dim() != 2 or tuple(gate.shape) != tuple(up.shape) or gate.shape[1] != hK:
+        raise ValueError(f"gate and up must both be [M, {hK}]")
+    if gate.device.index != hdev or up.device.index != hdev:
+        raise ValueError(f"inputs must be on cuda:{hdev}, where the weights are")
+    ok = (gate.dtype == torch.float32 and up.dtype == torch.float32 and gate.stride(1) == 1 and up.stride(1) == 1
+          and gate.stride(0) == up.stride(0) and gate.stride(0) % 4 == 0 and gate.data_ptr() % 16 == 0
+          and up.data_ptr() % 16 == 0)
+    if not ok:
+        gate = gate.to(torch.float32).contiguous().clone()
+        up = up.to(torch.float32).contiguous().clone()
+    M = gate.shape[0]
+    if out is None:
+        out = torch.empty((M, hN), dtype=torch.float32, device=gate.device)
+    if M == 0:
+        return out
+    with torch.cuda.device(gate.device):
+        stream = torch.cuda.current_stream(gate.device).cuda_stream
+        L.check(lib.ql_matmul_silu_mul_dev(ctypes.c_void_p(handle), gate.data_ptr(), up.data_ptr(),
+                                           int(gate.stride(0)), int(M), out.data_ptr(), stream), "silu_mul_matmul")
+    return out
+
+
 def concat_packed(handles):
     """One new handle stacking ``handles`` along N (same K, bits, scale type
     and zero points), e.g. gate and up, so projections that share an input run

@@ -761,6 +761,69 @@ QL_API int ql_matmul_rmsnorm_dev(void* handle, const float* dX, const float* dNo
     return run_compute(w, st->ws, M, dC, nullptr, s, hp, /*pdl=*/true);
 }
 
+// ------------------------------------------------------------------ fused SiLU * up prologue
+//
+// The reference decoder's MLP evaluates g1 = siluf(g1) * g2 into a scratch row
+// and then i4_matmul(md, g1) (kernel/qwen35_decoder.cpp:408-409), which re-reads
+// it to quantize it.  Here the quantizer reads the gate and up projections'
+// outputs and quantizes silu(gate) * up directly, with the reference's
+// arithmetic (ql_quant.cuh: the host library's expf method in double, then
+// x / (1 + e) and * up in fp32), so the product never round-trips through
+// memory unless the caller asks for it (dOut).
+namespace {
+int check_silu_args(const float* dG, const float* dU, int ld, int M, int K, const float* dOut) {
+    if (M < 0 || K <= 0 || K % 32 || ld < K || ld % 4) return QL_EINVAL;
+    if (M == 0) return QL_OK;
+    if (!dG || !dU) return QL_EINVAL;
+    if (reinterpret_cast<uintptr_t>(dG) % 16 || reinterpret_cast<uintptr_t>(dU) % 16 ||
+        reinterpret_cast<uintptr_t>(dOut) % 16)
+        return QL_EINVAL;        // 16-byte vector loads and stores
+    return QL_OK;
+}
+
+int run_quantize_silu(const float* dG, const float* dU, int ld, int M, int K, void* ws, float* dOut,
+                      cudaStream_t stream, bool hi_prec) {
+    const int nblk = K / 32;
+    if (use_gemm(M))
+        return cuda_status(launch_quantize_gemm_silu(dG, dU, ld, M, K, hi_prec, static_cast<uint8_t*>(ws), dOut,
+                                                     stream));
+    for (int c = 0; c * MAX_DECODE_TOKENS < M; ++c) {
+        const ActView act = chunk_view(ws, M, nblk, c, hi_prec);
+        const size_t m0 = static_cast<size_t>(c) * MAX_DECODE_TOKENS;
+        cudaError_t e = launch_quantize_act_silu(dG + m0 * ld, dU + m0 * ld, ld, act.M, K, hi_prec, act,
+                                                 dOut ? dOut + m0 * K : nullptr, stream);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    return set_status(QL_OK);
+}
+}  // namespace
+
+QL_API int ql_quantize_act_silu_mul_dev(const float* dGate, const float* dUp, int ld, int M, int K, int hi_prec,
+                                        void* ws, size_t ws_bytes, float* dOut, void* stream) {
+    const int c = check_silu_args(dGate, dUp, ld, M, K, dOut);
+    if (c != QL_OK || M == 0) return set_status(c);
+    if (!ws || reinterpret_cast<uintptr_t>(ws) % 16 || ws_bytes < ws_bytes_for(M, K / 32)) return set_status(QL_EINVAL);
+    return run_quantize_silu(dGate, dUp, ld, M, K, ws, dOut, static_cast<cudaStream_t>(stream), hi_prec != 0);
+}
+
+QL_API int ql_matmul_silu_mul_dev(void* handle, const float* dGate, const float* dUp, int ld, int M, float* dC,
+                                  void* stream) {
+    int c = check_call(handle, dGate, M, dC);
+    if (c != QL_OK || M == 0) return set_status(c);
+    const auto* w = static_cast<const Weight*>(handle);
+    c = check_silu_args(dGate, dUp, ld, M, w->K, nullptr);
+    if (c != QL_OK) return set_status(c);
+    const bool hp = ql_get_hi_prec() != 0;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* st = state_for(w->device);
+    cudaError_t e = ensure(&st->ws, &st->ws_bytes, ws_bytes_for(M, w->nblk));
+    if (e != cudaSuccess) return cuda_status(e);
+    const int rc = run_quantize_silu(dGate, dUp, ld, M, w->K, st->ws, nullptr, s, hp);
+    if (rc != QL_OK) return rc;
+    return run_compute(w, st->ws, M, dC, nullptr, s, hp, /*pdl=*/true);
+}
+
 // ------------------------------------------------------------------ concatenated weights
 //
 // Records are laid out row group by row group (rec[G][nblk][REC]), so stacking

@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(256) dequant_w16_kernel(const uint8_t* __restr
 // planes written as FP16: h = hi - 128 and l/256 (two-pass) or q8 (single-pass),
 // at plane p, K half kh, K column c (8 k each) and token tt of the tile:
 //   p*8192 + kh*4096 + c*2048 + (tt/8)*128 + (tt%8)*16.
-template <bool HP, bool NORM>
+template <bool HP, int PRO>
 __global__ void __launch_bounds__(256) quantize_f16_kernel(const float* __restrict__ A, int lda, int M, int K,
                                                            int m_tiles, uint8_t* __restrict__ out, NormArgs nrm) {
     pdl_launch_dependents();
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(256) quantize_f16_kernel(const float* __restri
         return;
     }
     float v[32];
-    load_block<NORM>(A, lda, m, b, nrm, v);
+    load_block<PRO>(A, lda, m, b, nrm, v);
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -606,11 +606,11 @@ cudaError_t launch_quantize_f16(const float* A, int lda, int M, int K, bool hi_p
     const unsigned grid = static_cast<unsigned>((total + 255) / 256);
     const NormArgs n = norm ? *norm : NormArgs{};
     if (norm) {
-        if (hi_prec) return launch_pdl_ex(quantize_f16_kernel<true, true>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
-        return launch_pdl_ex(quantize_f16_kernel<false, true>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
+        if (hi_prec) return launch_pdl_ex(quantize_f16_kernel<true, PRO_NORM>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
+        return launch_pdl_ex(quantize_f16_kernel<false, PRO_NORM>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
     }
-    if (hi_prec) return launch_pdl_ex(quantize_f16_kernel<true, false>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
-    return launch_pdl_ex(quantize_f16_kernel<false, false>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
+    if (hi_prec) return launch_pdl_ex(quantize_f16_kernel<true, PRO_NONE>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
+    return launch_pdl_ex(quantize_f16_kernel<false, PRO_NONE>, grid, 256, 0, stream, A, lda, M, K, m_tiles, out, n);
 }
 
 cudaError_t launch_gemmw(const Weight* w, const uint8_t* wd, const uint8_t* ad, int M, bool hi_prec, float* C,

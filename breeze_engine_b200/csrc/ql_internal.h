@@ -82,8 +82,10 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec);
 struct NormArgs {
     const float* row_inv;   // [M] 1/sqrt(mean(x^2) + eps), from launch_rmsnorm_factors
     const float* w;         // [K] norm weights
-    float* hn;              // [M][ldh] normalised rows, or nullptr
+    float* hn;              // [M][ldh] the values quantized (normalised rows, or silu * up), or nullptr
     int ldh;
+    const float* up;        // SiLU prologue: [M][ldu] up-projection output multiplying silu(A)
+    int ldu;
 };
 // row_inv[m] for M rows of X (ldx floats apart, K wide), ql_norm.cu.
 cudaError_t launch_rmsnorm_factors(const float* X, int ldx, int M, int K, float eps, float* row_inv,
@@ -155,6 +157,11 @@ constexpr size_t QL_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
                                 const ActView& out, cudaStream_t stream, const NormArgs* norm = nullptr);
+// The quantizers with the SiLU * up prologue (decode and GEMM layouts).
+cudaError_t launch_quantize_act_silu(const float* G, const float* U, int ld, int M, int K, bool hi_prec,
+                                     const ActView& out, float* dOut, cudaStream_t stream);
+cudaError_t launch_quantize_gemm_silu(const float* G, const float* U, int ld, int M, int K, bool hi_prec,
+                                      uint8_t* out, float* dOut, cudaStream_t stream);
 cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,
                                 float* ascale, cudaStream_t stream);
 cudaError_t launch_decode(const Weight* w, const ActView& act, bool hi_prec, float* C,

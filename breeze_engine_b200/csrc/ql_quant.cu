@@ -19,7 +19,7 @@
 
 namespace ql {
 
-template <bool HP, bool NORM>
+template <bool HP, int PRO>
 __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restrict__ A, int lda,
                                                            int M, int K, ActView out, NormArgs nrm) {
     // Let a dependent (PDL) kernel start its weight streaming right away; it
@@ -38,7 +38,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
         return;
     }
     float v[32];
-    load_block<NORM>(A, lda, m, b, nrm, v);
+    load_block<PRO>(A, lda, m, b, nrm, v);
     act_store_block<HP>(v, out, m, b);
 }
 
@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
 // s8; q8 in single-pass mode) and the lo plane (u8) as canonical K-major
 // tcgen05 B operands [2 K halves][8 groups of 8 tokens][8 tokens x 16 B], and
 // per (128-token tile, block) 128 fp32 scales.  Tokens M..(tile end) are zeros.
-template <bool HP, bool NORM>
+template <bool HP, int PRO>
 __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restrict__ A, int lda, int M, int K,
                                                             int m_tiles, uint8_t* __restrict__ out, NormArgs nrm) {
     pdl_launch_dependents();
@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) quantize_gemm_kernel(const float* __restr
         return;
     }
     float v[32];
-    load_block<NORM>(A, lda, m, b, nrm, v);
+    load_block<PRO>(A, lda, m, b, nrm, v);
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -135,11 +135,11 @@ cudaError_t launch_quantize_gemm(const float* A, int lda, int M, int K, bool hi_
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     const NormArgs n = norm ? *norm : NormArgs{};
     if (norm) {
-        if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, true>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
-        return launch_pdl(quantize_gemm_kernel<false, true>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+        if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, PRO_NORM>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+        return launch_pdl(quantize_gemm_kernel<false, PRO_NORM>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
     }
-    if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, false>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
-    return launch_pdl(quantize_gemm_kernel<false, false>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+    if (hi_prec) return launch_pdl(quantize_gemm_kernel<true, PRO_NONE>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
+    return launch_pdl(quantize_gemm_kernel<false, PRO_NONE>, grid, threads, stream, A, lda, M, K, m_tiles, out, n);
 }
 
 // Reference-layout variant for parity checks: hi/lo unsigned [M][K] (the
@@ -207,11 +207,36 @@ cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_p
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     const NormArgs n = norm ? *norm : NormArgs{};
     if (norm) {
-        if (hi_prec) return launch_pdl(quantize_act_kernel<true, true>, grid, threads, stream, A, lda, M, K, out, n);
-        return launch_pdl(quantize_act_kernel<false, true>, grid, threads, stream, A, lda, M, K, out, n);
+        if (hi_prec) return launch_pdl(quantize_act_kernel<true, PRO_NORM>, grid, threads, stream, A, lda, M, K, out, n);
+        return launch_pdl(quantize_act_kernel<false, PRO_NORM>, grid, threads, stream, A, lda, M, K, out, n);
     }
-    if (hi_prec) return launch_pdl(quantize_act_kernel<true, false>, grid, threads, stream, A, lda, M, K, out, n);
-    return launch_pdl(quantize_act_kernel<false, false>, grid, threads, stream, A, lda, M, K, out, n);
+    if (hi_prec) return launch_pdl(quantize_act_kernel<true, PRO_NONE>, grid, threads, stream, A, lda, M, K, out, n);
+    return launch_pdl(quantize_act_kernel<false, PRO_NONE>, grid, threads, stream, A, lda, M, K, out, n);
+}
+
+// SiLU * up prologue (the down projection's input): G and U are the gate and
+// up projections' outputs, ld floats per row; dOut (may be null, [M][K])
+// receives the values quantized.
+cudaError_t launch_quantize_act_silu(const float* G, const float* U, int ld, int M, int K, bool hi_prec,
+                                     const ActView& out, float* dOut, cudaStream_t stream) {
+    const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
+    const int threads = 256;
+    const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+    const NormArgs n{nullptr, nullptr, dOut, K, U, ld};
+    if (hi_prec) return launch_pdl(quantize_act_kernel<true, PRO_SILU>, grid, threads, stream, G, ld, M, K, out, n);
+    return launch_pdl(quantize_act_kernel<false, PRO_SILU>, grid, threads, stream, G, ld, M, K, out, n);
+}
+
+cudaError_t launch_quantize_gemm_silu(const float* G, const float* U, int ld, int M, int K, bool hi_prec,
+                                      uint8_t* out, float* dOut, cudaStream_t stream) {
+    const int m_tiles = (M + 127) / 128;
+    const long long total = static_cast<long long>(m_tiles) * 128 * (K / BLOCK_K);
+    const int threads = 256;
+    const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+    const NormArgs n{nullptr, nullptr, dOut, K, U, ld};
+    if (hi_prec)
+        return launch_pdl(quantize_gemm_kernel<true, PRO_SILU>, grid, threads, stream, G, ld, M, K, m_tiles, out, n);
+    return launch_pdl(quantize_gemm_kernel<false, PRO_SILU>, grid, threads, stream, G, ld, M, K, m_tiles, out, n);
 }
 
 cudaError_t launch_quantize_ref(const float* A, int M, int K, uint8_t* hi, uint8_t* lo,

@@ -51,13 +51,97 @@ __device__ __forceinline__ void norm_block(float (&v)[32], float r, const NormAr
     }
 }
 
-// The 32 values of (token m, block b): row m of A itself or, with the RMSNorm
-// prologue (NORM), normalised by the precomputed factor row_inv[m].
-template <bool NORM>
+// ---------------------------------------------------------------- SiLU * up prologue
+// The reference decoder's MLP input of the down projection is
+//     g1 = siluf(g1) * g2,  siluf(x) = x / (1.0f + expf(-x))
+// (kernel/qwen35_decoder.cpp:129, :408), with the host C library's expf.  That
+// expf is not correctly rounded; it is the published table-driven method in
+// double precision (k = round(x * 32/ln2) by adding and subtracting 1.5*2^52,
+// 2^(k/32) from a 32-entry table, a degree-3 polynomial in the reduced
+// argument, one rounding to float), built with fused multiply-adds on x86-64
+// CPUs with FMA.  expf_host_method() evaluates the same method with the same
+// fusions and roundings in explicit double operations, so it returns the
+// library's bits: oracle/expf_ref.c restates it on the host, and its checker
+// finds zero differences from the library over all 2^32 inputs.  The table
+// entries are the correctly rounded doubles of 2^(i/32), minus i << 47.
+static __device__ __constant__ unsigned long long EXP2_32_TAB[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+
+__device__ __forceinline__ float expf_host_method(float x) {
+    const double invln2_32 = 0x1.71547652b82fep+0 * 32;     // 32 / ln 2
+    const double shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;  // the method's minimax coefficients,
+    const double c1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;       // for the reduced argument in 1/32 units
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t top = (ux >> 20) & 0x7ffu;
+    if (top >= ((0x42B00000u >> 20) & 0x7ffu)) {            // |x| >= 88 (0x42B00000 = 88.0f), NaN, inf
+        if (ux == 0xFF800000u) return 0.0f;                 // -inf
+        if (top >= 0x7f8u) return __fadd_rn(x, x);          // NaN, +inf
+        if (x > 0x1.62e42ep6f) return __uint_as_float(0x7F800000u);   // above log(2^128): +inf
+        if (x < -0x1.9fe368p6f) return 0.0f;                           // below log(2^-150)
+    }
+    const double xd = static_cast<double>(x);
+    double kd = __fma_rn(invln2_32, xd, shift);             // x*32/ln2 rounded to an integer (+ shift)
+    const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(invln2_32, xd, -kd);          // reduced argument, unrounded product
+    const unsigned long long t = EXP2_32_TAB[ki & 31] + (ki << 47);
+    const double s = __longlong_as_double(static_cast<long long>(t));
+    const double z = __fma_rn(c0, r, c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(c2, r, 1.0);
+    y = __fma_rn(z, r2, y);
+    y = __dmul_rn(y, s);
+    return __double2float_rn(y);
+}
+
+// silu(g) * u as the reference evaluates it: x / (1 + expf(-x)), then * u,
+// every operation one rounding.
+__device__ __forceinline__ float silu_mul_ref(float g, float u) {
+    const float e = expf_host_method(-g);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+}
+
+// Activation prologues of the quantizers: 0 = A as it is, 1 = the RMSNorm
+// (NormArgs row_inv and w), 2 = silu(A) * up (NormArgs up / ldu: the gate
+// projection's output in A, the up projection's in `up`).  With a prologue the
+// values quantized can also be written out (NormArgs hn / ldh).
+enum : int { PRO_NONE = 0, PRO_NORM = 1, PRO_SILU = 2 };
+
+__device__ __forceinline__ void silu_block(float (&v)[32], const NormArgs& nrm, int m, int b) {
+    const float4* u4 = reinterpret_cast<const float4*>(nrm.up + static_cast<size_t>(m) * nrm.ldu + b * BLOCK_K);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 u = __ldg(u4 + i);
+        v[4 * i + 0] = silu_mul_ref(v[4 * i + 0], u.x);
+        v[4 * i + 1] = silu_mul_ref(v[4 * i + 1], u.y);
+        v[4 * i + 2] = silu_mul_ref(v[4 * i + 2], u.z);
+        v[4 * i + 3] = silu_mul_ref(v[4 * i + 3], u.w);
+    }
+    if (nrm.hn) {
+        float4* dst = reinterpret_cast<float4*>(nrm.hn + static_cast<size_t>(m) * nrm.ldh + b * BLOCK_K);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+}
+
+// The 32 values of (token m, block b): row m of A itself, or with a prologue
+// (PRO) normalised by the precomputed factor row_inv[m] or as silu(A) * up.
+template <int PRO>
 __device__ __forceinline__ void load_block(const float* __restrict__ A, int lda, int m, int b,
                                            const NormArgs& nrm, float (&v)[32]) {
     load_raw_block(A, lda, m, b, v);
-    if (NORM) norm_block(v, __ldg(nrm.row_inv + m), nrm, m, b);
+    if (PRO == PRO_NORM) norm_block(v, __ldg(nrm.row_inv + m), nrm, m, b);
+    if (PRO == PRO_SILU) silu_block(v, nrm, m, b);
 }
 
 // Decode-layout record of (token m, block b): the four fragment slots of

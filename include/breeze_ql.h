@@ -201,6 +201,27 @@ int ql_quantize_act_rmsnorm_dev(const float* dX, const float* dNormW, float eps,
 int ql_matmul_rmsnorm_dev(void* handle, const float* dX, const float* dNormW, float eps, int M,
                           float* dC, void* stream);
 
+/* Fused SiLU * up prologue (no counterpart in the reference's C ABI; it
+ * replaces the reference decoder's g1 = siluf(g1) * g2 loop before its down
+ * projection, kernel/qwen35_decoder.cpp:408-409, siluf at :129): the values
+ * quantized are silu(gate) * up element by element,
+ *   x / (1.0f + expf(-x)) * u,
+ * with the host C library's expf reproduced bit for bit (the same method and
+ * roundings in double precision, checked against the library over all 2^32
+ * inputs), so the result equals i4_matmul(handle, g1, M, C) on the reference's
+ * own g1.  dGate and dUp are [M, K] with rows `ld` floats apart (ld >= K,
+ * ld % 4 == 0; e.g. the halves of a concatenated gate|up output, ld = 2K,
+ * dUp = dGate + K), 16-byte aligned, K % 32 == 0.
+ * ql_quantize_act_silu_mul_dev: the split form of ql_quantize_act_dev (then
+ * ql_matmul_quantized_dev) with a workspace of >= ql_act_workspace_bytes(M, K)
+ * bytes; dOut (16-byte aligned, may be NULL) receives the products [M, K].
+ * ql_matmul_silu_mul_dev: one call with the library's workspace and the
+ * process-wide activation mode (i4_set_hi_prec). */
+int ql_quantize_act_silu_mul_dev(const float* dGate, const float* dUp, int ld, int M, int K, int hi_prec,
+                                 void* ws, size_t ws_bytes, float* dOut, void* stream);
+int ql_matmul_silu_mul_dev(void* handle, const float* dGate, const float* dUp, int ld, int M, float* dC,
+                           void* stream);
+
 /* One handle stacking `count` weights along N (no counterpart in the
  * reference, which calls i4_matmul once per projection that shares an input,
  * e.g. gate and up at kernel/qwen35_decoder.cpp:406-407).  All handles need

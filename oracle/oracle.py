@@ -89,6 +89,11 @@ class Oracle:
         lib.ql_oracle_matmul.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp]
         lib.ql_oracle_matmul_i8.argtypes = [_vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp]
         lib.ql_oracle_rmsnorm.argtypes = [_vp, _vp, _i, _i, ctypes.c_float, _vp]
+        lib.ql_expf_restated.restype = ctypes.c_float
+        lib.ql_expf_restated.argtypes = [ctypes.c_float, _i]
+        lib.ql_silu_mul_array.argtypes = [_vp, _vp, _vp, ctypes.c_longlong]
+        lib.ql_expf_check.restype = ctypes.c_ulonglong
+        lib.ql_expf_check.argtypes = [ctypes.c_uint32, ctypes.c_uint32, _i, ctypes.POINTER(ctypes.c_uint32)]
         self.lib = lib
 
     def quantize_i16(self, a):
@@ -136,6 +141,24 @@ class Oracle:
         return c
 
 
+    def silu_mul(self, g, u):
+        """silu(g) * u element by element as the reference decoder computes it
+        (``kernel/qwen35_decoder.cpp:129, 408``), on the restated exponential
+        of ``expf_ref.c``."""
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        assert g.shape == u.shape
+        out = np.empty_like(g)
+        self.lib.ql_silu_mul_array(_p(g), _p(u), _p(out), g.size)
+        return out
+
+    def expf_check(self, lo=0, hi=0xFFFFFFFF, fused=True):
+        """(mismatches, first mismatching bit pattern) of the restated expf
+        against this host's C library over the float bit patterns lo..hi."""
+        first = ctypes.c_uint32()
+        bad = self.lib.ql_expf_check(lo, hi, 1 if fused else 0, ctypes.byref(first))
+        return int(bad), int(first.value)
+
     def rmsnorm(self, x, w, eps):
         """hn = rmsnorm(x) as the reference decoder computes it
         (``kernel/qwen35_decoder.cpp:133-141``)."""
@@ -164,6 +187,7 @@ class Reference:
         lib.refprobe_replay.argtypes = [_vp, _vp, _vp, _i, _vp]
         lib.refprobe_replay.restype = _i
         lib.refprobe_rmsnorm.argtypes = [_vp, _vp, _vp, _i, _i, ctypes.c_float]
+        lib.refprobe_silu_mul.argtypes = [_vp, _vp, _vp, ctypes.c_longlong]
         self.lib = lib
         lib.i4_set_numa_split(1 << 30)
 
@@ -212,6 +236,16 @@ class Reference:
         cs = np.empty((M, N, K // 32), np.int32)
         assert self.lib.refprobe_block_sums(_vp(handle), _p(hi), _p(lo), M, _p(cs)) == 0
         return cs
+
+    def silu_mul(self, g, u):
+        """The reference decoder's own ``siluf(g) * u`` (``kernel/qwen35_decoder.cpp:129, 408``),
+        compiled from its source file by ``oracle/ref_norm_probe.cpp``."""
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        assert g.shape == u.shape
+        out = np.empty_like(g)
+        self.lib.refprobe_silu_mul(_p(out), _p(g), _p(u), g.size)
+        return out
 
     def rmsnorm(self, x, w, eps):
         """The reference decoder's own rmsnorm (``kernel/qwen35_decoder.cpp:133-141``),

@@ -203,3 +203,49 @@ def norm_digest(x, w, eps):
     for v in (x, w, np.float32(eps)):
         h.update(np.ascontiguousarray(v).tobytes())
     return h.hexdigest()
+
+
+def _neighbours(values, radius):
+    """Every float within `radius` ulps of each value (by bit pattern)."""
+    out = []
+    for v in values:
+        u = int(np.array([v], np.float32).view(np.uint32)[0])
+        out.append(np.arange(u - radius, u + radius + 1, dtype=np.int64).astype(np.uint32).view(np.float32))
+    return np.concatenate(out)
+
+
+def silu_cases():
+    """(gate, up) pairs for the SiLU * up prologue of the down projection
+    (the reference decoder's ``g1 = siluf(g1) * g2``,
+    ``kernel/qwen35_decoder.cpp:129, 408``): MLP-like values, the whole range of
+    the exponential, and its edges -- overflow and underflow thresholds, the
+    two inputs near float rounding midpoints where the C library's expf and a
+    plain (unfused) evaluation of its method differ (32.5646324 and
+    -63.0994606, reached as -g) with their neighbours, zeros, subnormals,
+    infinities and NaN.  Every case is [M, K] with K % 32 == 0."""
+    cases = {}
+    rng = np.random.default_rng(31)
+    cases["mlp_k4096"] = ((rng.normal(size=(8, 4096)) * 2.0).astype(np.float32),
+                          (rng.normal(size=(8, 4096)) * 2.0).astype(np.float32))
+    g = rng.uniform(-110.0, 110.0, size=(4, 2048)).astype(np.float32)
+    cases["range_k2048"] = (g, rng.normal(size=(4, 2048)).astype(np.float32))
+    special = np.array([-32.564632415771484, 63.09946060180664, 32.564632415771484, -63.09946060180664,
+                        -88.72283935546875, -88.72284698486328, 88.0, -88.0, 103.97207641601562,
+                        103.97208404541016, 87.3365478515625, -87.3365478515625, 0.0, -0.0, 1e-40, -1e-40,
+                        np.inf, -np.inf, np.nan, 3e38, -3e38, 1e-30, -1e-30, 0.5, -0.5, 20.0, -20.0],
+                       np.float32)
+    edge = np.concatenate([special, _neighbours(special[:4], 200), _neighbours(special[4:12], 20)])
+    k = ((edge.size + 31) // 32) * 32
+    e = np.zeros(k, np.float32)
+    e[: edge.size] = edge
+    u = np.random.default_rng(32).normal(size=k).astype(np.float32)
+    u[:32] = 1.0
+    cases["edges"] = (e.reshape(1, k), u.reshape(1, k))
+    return cases
+
+
+def silu_digest(g, u):
+    h = hashlib.sha256()
+    for v in (g, u):
+        h.update(np.ascontiguousarray(v).tobytes())
+    return h.hexdigest()

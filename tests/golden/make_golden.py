@@ -14,10 +14,13 @@ on every case of ``cases.py``, and stores:
 It also runs the reference decoder's own ``rmsnorm``
 (``kernel/qwen35_decoder.cpp:133-141``, exported by ``oracle/ref_norm_probe.cpp``)
 on ``cases.norm_cases()`` and stores ``<case>/digest`` and ``<case>/hn`` in
-``golden_norm.npz``.
+``golden_norm.npz``, and its ``siluf(g) * u`` (``kernel/qwen35_decoder.cpp:129,
+408``, the same probe file) on ``cases.silu_cases()``, storing ``<case>/digest``
+and ``<case>/y`` in ``golden_silu.npz``.
 
 Run from the repository root where the reference checkout exists:
-``python tests/golden/make_golden.py [--norm-only]``.
+``python tests/golden/make_golden.py [--norm-only]`` (``--norm-only`` writes the
+norm and SiLU fixtures only).
 """
 import os
 import sys
@@ -28,7 +31,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
-from cases import all_cases, input_digest, norm_cases, norm_digest  # noqa: E402
+from cases import all_cases, input_digest, norm_cases, norm_digest, silu_cases, silu_digest  # noqa: E402
 from oracle.oracle import Reference, build  # noqa: E402
 
 CS_LIMIT = 10_000    # store INT32 accumulators when M*N*nblk is at most this
@@ -45,10 +48,22 @@ def make_norm(ref):
     print(f"wrote {path} ({os.path.getsize(path)} bytes)")
 
 
+def make_silu(ref):
+    out = {}
+    for name, (g, u) in silu_cases().items():
+        out[f"{name}/digest"] = np.frombuffer(bytes.fromhex(silu_digest(g, u)), np.uint8)
+        out[f"{name}/y"] = ref.silu_mul(g, u)
+        print(f"silu {name}: {g.shape}")
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_silu.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+
+
 def main():
     build()
     ref = Reference()
     make_norm(ref)
+    make_silu(ref)
     if "--norm-only" in sys.argv[1:]:
         return
     out = {}

@@ -149,3 +149,53 @@ def concat(handles):
     rc = lib().ql_weight_concat(arr, len(handles), ctypes.byref(out))
     assert rc == 0 and out.value, lib().ql_error_string(rc)
     return out.value
+
+
+def silu_quantize_dev(g, u, hi_prec, ld=None):
+    """ql_quantize_act_silu_mul_dev: returns (workspace tensor, the products).
+    With ld > K, gate and up sit side by side in one [M, ld] buffer (up at
+    column K, as in a concatenated gate|up output)."""
+    import torch
+    g = np.ascontiguousarray(g, np.float32)
+    u = np.ascontiguousarray(u, np.float32)
+    M, K = g.shape
+    ld = ld or K
+    if ld == K:
+        buf = np.concatenate([g, u], axis=0)          # separate planes: gate rows, then up rows
+    else:
+        buf = np.zeros((M, ld), np.float32)
+        buf[:, :K] = g
+        buf[:, K:2 * K] = u
+    dbuf = torch.from_numpy(np.ascontiguousarray(buf)).cuda()
+    if ld == K:
+        dG, dU = dbuf[:M], dbuf[M:]
+    else:
+        dG, dU = dbuf[:, :K], dbuf[:, K:2 * K]
+    need = lib().ql_act_workspace_bytes(M, K)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    out = torch.full((M, K), -7.0, dtype=torch.float32, device="cuda")
+    rc = lib().ql_quantize_act_silu_mul_dev(dG.data_ptr(), dU.data_ptr(), ld, M, K, 1 if hi_prec else 0,
+                                            ws.data_ptr(), need, out.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return ws, out.cpu().numpy()
+
+
+def matmul_silu_dev(h, g, u, N, ld_pad=0):
+    """ql_matmul_silu_mul_dev (library workspace, process-wide activation mode),
+    gate and up in one [M, 2K + ld_pad] buffer."""
+    import torch
+    g = np.ascontiguousarray(g, np.float32)
+    M, K = g.shape
+    ld = 2 * K + ld_pad
+    buf = np.zeros((M, ld), np.float32)
+    buf[:, :K] = g
+    buf[:, K:2 * K] = u
+    dbuf = torch.from_numpy(buf).cuda()
+    dC = torch.full((M, N), -12345.0, dtype=torch.float32, device="cuda")
+    rc = lib().ql_matmul_silu_mul_dev(_vp(h), dbuf.data_ptr(), dbuf[:, K:].data_ptr(), ld, M, dC.data_ptr(),
+                                      torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().ql_error_string(rc)
+    torch.cuda.synchronize()
+    return dC.cpu().numpy()
