@@ -16,8 +16,9 @@ Workloads (``--workload``):
   two-pass INT16.  One step is the 3 calls.  ``value`` is INT8 tera-operations
   per second counted as the headline metric does: ``4*M*N*K`` per call (two
   INT8 passes of 2*M*N*K each).  The default ``decode`` line also carries this
-  workload's measurement under ``secondary.prefill`` (``--no-secondary`` skips
-  it), so one driver run measures both halves of the metric.
+  workload's measurement under ``secondary.prefill``, and configs[3]'s INT4
+  layer set at M = 1 under ``secondary.layer_m1`` (``--no-secondary`` skips
+  both), so one driver run measures both halves of the metric.
 * ``mlp_front``: the front of a Qwen3.5-27B MLP block at decode batch sizes
   (M in {1, 4, 8, 16}; H = 5120, intermediate 17408, INT4 with fp16 scales):
   the RMSNorm fused into the activation quantizer, then one decode launch over
@@ -319,7 +320,7 @@ class DecodeWorkload:
         peak, kind = measured_peaks()
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
-        if os.path.exists(tpath):
+        if self.name == "decode" and os.path.exists(tpath):     # captured on the INT8 sweep
             try:
                 tr = json.load(open(tpath))
                 traffic = round(tr["dram_bytes"] / tr["alg_bytes"] * kern_amount_avg)
@@ -432,7 +433,8 @@ class _OpsOrBytes:
 
     def __init__(self):
         self.unit = "GB/s" if self.M <= 64 else "TOPS"
-        self.kernel = ("decode_kernel (ql_gemv.cu)" if self.M <= 64
+        self.kernel = ("decode_dp4a_kernel (ql_gemv4.cu) for layers of >= 8192 rows at M <= 2, "
+                       "decode_kernel (ql_gemv.cu) otherwise" if self.M <= 64
                        else "gemmw_kernel (ql_gemmw.cu, tcgen05 kind::f16 on per-call FP16-dequantized weights)")
 
     def step_amount(self, calls):
@@ -793,13 +795,15 @@ def run_ours(args):
     backend.set_hi_prec(True)
     line = _measure(args, WORKLOADS[args.workload](), lib, rank, local_rank, world)
     # The headline metric names both halves of the path: the default decode
-    # line also carries configs[2]'s prefill GEMM, measured the same way.
+    # line also carries configs[2]'s prefill GEMM and configs[3]'s INT4 layer set
+    # at one token (the 27B-class decode shapes), measured the same way.
     if args.workload == "decode" and not args.no_secondary:
-        sec = _measure(args, PrefillWorkload(), lib, rank, local_rank, world)
-        if rank == 0:
-            keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "e2e",
-                    "cpu_baseline", "gpu_launches", "clocks")
-            line["secondary"] = {"prefill": {k: sec[k] for k in keep if k in sec}}
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "e2e",
+                "cpu_baseline", "gpu_launches", "clocks")
+        for name, make in (("prefill", PrefillWorkload), ("layer_m1", lambda: LayerSetWorkload(1))):
+            sec = _measure(args, make(), lib, rank, local_rank, world)
+            if rank == 0:
+                line.setdefault("secondary", {})[name] = {k: sec[k] for k in keep if k in sec}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1329,7 +1333,7 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
-                    help="decode workload: skip the configs[2] prefill measurement in `secondary`")
+                    help="decode workload: skip the configs[2] / configs[3] measurements in `secondary`")
     ap.add_argument("--ncu-case", metavar="K,N,BITS,M", default=None,
                     help="profiling driver: pack one layer, quantize once, run the matmul kernel "
                          "4 times and exit (for ncu captures of a single launch)")
