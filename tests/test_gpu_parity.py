@@ -332,3 +332,52 @@ def test_dp4a_decode_kernel(zp, half, hp, K, oracle):
                 assert np.array_equal(qlc.block_sums_dev(h, a, N, K), oracle.block_sums(qw, qz, N, K, 4, hi, lo))
     finally:
         qlc.free(h)
+
+
+@pytest.mark.parametrize("zp,half", [(False, True), (True, True), (True, False), (False, False)])
+@pytest.mark.parametrize("hp", [True, False])
+@pytest.mark.parametrize("N,K", [(16, 32), (48, 800), (1040, 5120), (5120, 17408)])
+def test_dp4a_chain_kernel(zp, half, hp, N, K, oracle):
+    """INT4 at one and two tokens on layers of fewer than 8192 rows run the
+    chain variant of the dp4a decode kernel (one row group per CTA, f values
+    through a shared-memory ring, one warp running the ordered FP32 chain):
+    bit-exact against the oracle from one row group and one block up to the
+    27B-class down projection (17408 x 5120), with explicit zero points,
+    fp16/fp32 scales, both activation modes and edge-valued activations."""
+    from cases import edge_activations
+    qw, sc, qz = _weights(N, K, 4, zp, half, N + K + 2 * zp + half)
+    h = qlc.prepack(qw, sc, qz, N, K, 4)
+    qlc.set_hi_prec(hp)
+    try:
+        for M in (1, 2):
+            a = np.random.default_rng(M + K).standard_normal((M, K)).astype(np.float32)
+            if K >= 800:
+                a[:, : K // 4] = edge_activations(M, K // 4, 3)
+            assert bits_equal(qlc.matmul_dev(h, a, N), oracle.matmul(qw, sc, qz, N, K, 4, a, hi_prec=hp)), M
+    finally:
+        qlc.free(h)
+        qlc.set_hi_prec(False)
+
+
+@pytest.mark.parametrize("cfg", ["1,4,16,4,4", "2,4,16,0,0", "4,4,16,0,0", "1,2,5,2,2", "2,8,7,8,8",
+                                 "4,1,3,1,1", "1,3,16,6,3", "4,4,24,4,4"])
+@pytest.mark.parametrize("N", [1008, 8208])
+def test_dp4a_chain_configs(cfg, N, oracle, monkeypatch):
+    """Every carve-up of the chain kernel gives the same bits: one, two or
+    four row groups per CTA (a partial last CTA when N / 16 is not a multiple),
+    one to eight consumer warps, stages of 3 to 32 blocks (partial last
+    stages), rings from one slot to eight that wrap many times; on a small
+    layer and, forced with BREEZE_QL_DP4A_KERNEL=chain, on a wide one."""
+    K = 2848                        # 89 blocks: no stage size divides it
+    qw, sc, qz = _weights(N, K, 4, True, True, 9)
+    h = qlc.prepack(qw, sc, qz, N, K, 4)
+    qlc.set_hi_prec(True)
+    monkeypatch.setenv("BREEZE_QL_DP4A_KERNEL", "chain")
+    monkeypatch.setenv("BREEZE_QL_DP4A_CHAIN", cfg)
+    try:
+        for M in (1, 2):
+            a = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+            assert bits_equal(qlc.matmul_dev(h, a, N), oracle.matmul(qw, sc, qz, N, K, 4, a, hi_prec=True)), M
+    finally:
+        qlc.free(h)
+        qlc.set_hi_prec(False)
