@@ -302,7 +302,11 @@ __global__ void __launch_bounds__(288) decode_dp4a_kernel(const Dp4aParams p) {
 // down projections of a 27B-class layer).  A CTA owns R (1, 2 or 4) row groups
 // over the whole K range, so the grid has G / R CTAs instead of G / 4, and the
 // ordered FP32 chain leaves the consumers:
-//   * the producer warp streams stages of BPS blocks as above;
+//   * PROD producer warps stream stages of BPS blocks as above, producer p
+//     the stages p, p + PROD, ... (measured on B200: one issuing thread's
+//     bulk copies stream at most ~16-19 GB/s however deep its ring, two
+//     ~26 GB/s and four ~31 GB/s, so a CTA that owns one row group needs
+//     several to keep HBM busy);
 //   * consumer warp w takes stages w, w + CONS, ...; its lanes cover four
 //     (row group, block) units per pass (lane = 8 * unit + g; a unit is one
 //     record, 4 / R blocks of each of the R row groups per pass) and write the
@@ -323,12 +327,13 @@ struct ChainParams {
     int* err;
     int M, N, nblk, G, ldc;
     int TPB, TPBA, QREC;
-    int R, CONS, BPS, STAGES, FS;   // row groups per CTA, consumer warps, blocks per stage, ring depths
+    int R, CONS, PROD, BPS, STAGES, FS;   // row groups per CTA, consumer and producer warps, blocks per
+                                          // stage, ring depths
     uint32_t stage_bytes, off_Q, off_f, fslot_floats, fstr, off_stages;
 };
 
 template <bool HALF, bool ZP, int MTOK, bool HP>
-__global__ void __launch_bounds__(320) decode_dp4a_chain_kernel(const ChainParams p) {
+__global__ void __launch_bounds__(416) decode_dp4a_chain_kernel(const ChainParams p) {
     constexpr int REC = 256 + (HALF ? 32 : 64) + (ZP ? 16 : 0);
     constexpr int LB = HP ? 16 : 8;
     constexpr int PU = 4;                           // passes held in registers before the stores
@@ -362,9 +367,12 @@ __global__ void __launch_bounds__(320) decode_dp4a_chain_kernel(const ChainParam
     __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == p.CONS + 1) {
-        // ------------------------------------------------------------ producer
+    if (warp > p.CONS) {
+        // ----------------------------------------------------------- producers
+        // producer pr issues the stages i = pr (mod PROD) and, as STAGES is a
+        // multiple of PROD, waits only on ring slots it filled itself
         if (lane != 0) return;
+        const int pr = warp - p.CONS - 1;
         auto issue = [&](int i, bool weights, bool acts) {
             const int s = i % p.STAGES;
             const uint32_t base = smem_u32(stages + static_cast<size_t>(s) * p.stage_bytes);
@@ -381,14 +389,14 @@ __global__ void __launch_bounds__(320) decode_dp4a_chain_kernel(const ChainParam
             if (acts) bulk_g2s(base + p.off_Q, p.q + static_cast<size_t>(b0) * p.QREC, nb * p.QREC, full);
         };
         const int first = min(p.STAGES, nst);
-        for (int i = 0; i < first; ++i) issue(i, true, false);
+        for (int i = pr; i < first; i += p.PROD) issue(i, true, false);
         pdl_wait();                                   // activations come from the previous grid
-        for (int i = 0; i < first; ++i) issue(i, false, true);
-        for (int i = first; i < nst; ++i) {
+        for (int i = pr; i < first; i += p.PROD) issue(i, false, true);
+        for (int i = first + ((pr - first) % p.PROD + p.PROD) % p.PROD; i < nst; i += p.PROD) {
             const int s = i % p.STAGES;
             if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) {
-                for (int j = max(0, i - p.STAGES); j < i; ++j)      // let issued copies land
-                    if (!mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
+                for (int j = i - p.STAGES; j < i; j += p.PROD)       // let this producer's copies land
+                    if (j >= 0 && !mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
                 return;
             }
             issue(i, true, true);
@@ -636,36 +644,39 @@ cudaError_t d4_dispatch(const Weight* w, const Dp4aParams& p, int M, cudaStream_
 // ---------------------------------------------------------------- chain variant
 
 struct ChainConfig {
-    int R, CONS, BPS, STAGES, FS;
+    int R, CONS, PROD, BPS, STAGES, FS;
 };
 
 int chain_fstr(int BPS) { return ((BPS + 15) & ~15) + 4; }
 int chain_fslot_floats(int R, int BPS, int mtok) { return mtok * (16 * R + 1) * chain_fstr(BPS); }
 
-// One row group per CTA, four consumer warps, stages of 32 blocks; the ring as
-// deep as the shared memory of the CTAs that share an SM allows (up to three
-// per SM), at most 32 stages and no deeper than the K range needs.  Measured
-// on B200 (INT4, one token, the 27B-class attention and down projections):
-// stages of 32 blocks beat 16 and 8 on every layer, and two or eight consumer
-// warps, or two row groups per CTA, were no faster than this.
+// One row group per CTA, four consumer and four producer warps, stages of 32
+// blocks; the ring as deep as the shared memory of the CTAs that share an SM
+// allows (up to three per SM), at most 32 stages and no deeper than the K range
+// needs.  Measured on B200 (INT4, one token, the 27B-class attention and down
+// projections): stages of 32 blocks beat 16 and 8 on every layer; four
+// producers took 3-6% off the 5120-row layers against one (three, which forces
+// a 12-deep ring, was much slower); two or eight consumer warps, or two row
+// groups per CTA, were no faster.
 ChainConfig chain_plan(int G, int nblk, int rec, int qrec, int mtok) {
     const int sms = d4_sms();
     ChainConfig c;
     c.R = 1;
     c.CONS = 4;
+    c.PROD = 4;
     c.BPS = 32;
     c.FS = 8;
-    if (const char* env = std::getenv("BREEZE_QL_DP4A_CHAIN")) {       // "R,CONS,BPS,STAGES,FS", 0 = planner
-        int r = 0, co = 0, b = 0, st = 0, fs = 0;
-        if (std::sscanf(env, "%d,%d,%d,%d,%d", &r, &co, &b, &st, &fs) == 5) {
+    c.STAGES = 0;
+    if (const char* env = std::getenv("BREEZE_QL_DP4A_CHAIN")) {   // "R,CONS,BPS,STAGES,FS[,PROD]", 0 = planner
+        int r = 0, co = 0, b = 0, st = 0, fs = 0, pd = 0;
+        if (std::sscanf(env, "%d,%d,%d,%d,%d,%d", &r, &co, &b, &st, &fs, &pd) >= 5) {
             if (r > 0) c.R = r;
             if (co > 0) c.CONS = co;
             if (b > 0) c.BPS = b;
             if (fs > 0) c.FS = fs;
+            if (pd > 0) c.PROD = pd;
             c.STAGES = st;
         }
-    } else {
-        c.STAGES = 0;
     }
     if (c.STAGES <= 0) {
         const long long ctas = (G + c.R - 1) / c.R;
@@ -675,11 +686,13 @@ ChainConfig chain_plan(int G, int nblk, int rec, int qrec, int mtok) {
         const int fixed = 256 + c.FS * fslot * 4 + 256;
         const int stage = d4_stage_bytes(c.R, c.BPS, rec, qrec);
         const int nst = (nblk + c.BPS - 1) / c.BPS;
+        const int unit = std::max(c.CONS, c.PROD) % std::min(c.CONS, c.PROD) == 0 ? std::max(c.CONS, c.PROD)
+                                                                                 : c.CONS * c.PROD;
         int st = (budget - fixed) / stage;
         st = std::min(st, 32);
-        st = std::min(st, ((nst + c.CONS - 1) / c.CONS) * c.CONS);
-        st = (st / c.CONS) * c.CONS;
-        c.STAGES = std::max(st, c.CONS);
+        st = std::min(st, ((nst + unit - 1) / unit) * unit);
+        st = (st / unit) * unit;
+        c.STAGES = std::max(st, unit);
     }
     return c;
 }
@@ -703,6 +716,7 @@ cudaError_t chain_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     p.QREC = p0.QREC;
     p.R = c.R;
     p.CONS = c.CONS;
+    p.PROD = c.PROD;
     p.BPS = c.BPS;
     p.STAGES = c.STAGES;
     p.FS = c.FS;
@@ -717,8 +731,9 @@ cudaError_t chain_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     // the carve-up must fit the SM and keep the invariants the kernel relies on:
     // a stage and an f-slot return to the warp that used them last, and a warp
     // pass covers four (row group, block) units
-    if (smem > 227 * 1024 || (c.R != 1 && c.R != 2 && c.R != 4) || c.CONS < 1 || c.CONS > 8 || c.BPS < 1 ||
-        c.STAGES < 1 || c.FS < 1 || (c.STAGES % c.CONS) || (c.FS % c.CONS) || (p.QREC % 16) || (REC % 16))
+    if (smem > 227 * 1024 || (c.R != 1 && c.R != 2 && c.R != 4) || c.CONS < 1 || c.CONS > 8 || c.PROD < 1 ||
+        c.PROD > 4 || c.BPS < 1 || c.STAGES < 1 || c.FS < 1 || (c.STAGES % c.CONS) || (c.STAGES % c.PROD) ||
+        (c.FS % c.CONS) || (p.QREC % 16) || (REC % 16))
         return cudaErrorInvalidConfiguration;
     auto kern = decode_dp4a_chain_kernel<HALF, ZP, MTOK, HP>;
     static int configured[64] = {0};
@@ -732,7 +747,7 @@ cudaError_t chain_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.G + c.R - 1) / c.R);
-    cfg.blockDim = dim3(32 * (c.CONS + 2));
+    cfg.blockDim = dim3(32 * (c.CONS + 1 + c.PROD));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -359,15 +359,16 @@ def test_dp4a_chain_kernel(zp, half, hp, N, K, oracle):
         qlc.set_hi_prec(False)
 
 
-@pytest.mark.parametrize("cfg", ["1,4,16,4,4", "2,4,16,0,0", "4,4,16,0,0", "1,2,5,2,2", "2,8,7,8,8",
-                                 "4,1,3,1,1", "1,3,16,6,3", "4,4,24,4,4"])
+@pytest.mark.parametrize("cfg", ["1,4,16,4,4,1", "2,4,16,0,0,2", "4,4,16,0,0,4", "1,2,5,2,2,2", "2,8,7,8,8,4",
+                                 "4,1,3,1,1,1", "1,3,16,6,3,3", "4,4,24,4,4,2", "1,4,32,0,8,4", "1,4,8,12,4,3"])
 @pytest.mark.parametrize("N", [1008, 8208])
 def test_dp4a_chain_configs(cfg, N, oracle, monkeypatch):
     """Every carve-up of the chain kernel gives the same bits: one, two or
     four row groups per CTA (a partial last CTA when N / 16 is not a multiple),
-    one to eight consumer warps, stages of 3 to 32 blocks (partial last
-    stages), rings from one slot to eight that wrap many times; on a small
-    layer and, forced with BREEZE_QL_DP4A_KERNEL=chain, on a wide one."""
+    one to eight consumer warps, one to four producer warps, stages of 3 to
+    32 blocks (partial last stages), rings from one slot to twelve that wrap
+    many times; on a small layer and, forced with BREEZE_QL_DP4A_KERNEL=chain,
+    on a wide one."""
     K = 2848                        # 89 blocks: no stage size divides it
     qw, sc, qz = _weights(N, K, 4, True, True, 9)
     h = qlc.prepack(qw, sc, qz, N, K, 4)
