@@ -368,7 +368,8 @@ QL_API int ql_device_error(int clear) {
 // them as soon as the call returns.
 QL_API void* i4_prepack_onnx(const uint8_t* qw, const void* scales, const uint8_t* qzeros, int N,
                              int K, int bits, int scale_bits) {
-    if (!qw || !scales || (scale_bits != 16 && scale_bits != 32) || (bits == 8 && qzeros)) {
+    if (!qw || !scales || (scale_bits != 16 && scale_bits != 32) || (bits == 8 && qzeros) || N <= 0 || K <= 0 ||
+        N % 16 || K % 32 || (bits != 4 && bits != 8)) {
         set_status(QL_EINVAL);
         return nullptr;
     }
@@ -442,7 +443,7 @@ QL_API int ql_prepack_onnx_dev(const uint8_t* d_qw, const void* d_scales, const 
 QL_API void* i4_prepack(const uint8_t* srcB, const float* srcScale, const int8_t* srcZp,
                         const int32_t* srcCorr, int N, int K, int nblk, int bits) {
     if (!srcB || !srcScale || !srcCorr || (bits == 4 && !srcZp) || nblk != K / 32 || N <= 0 ||
-        K <= 0 || N % 16 || K % 32) {
+        K <= 0 || N % 16 || K % 32 || (bits != 4 && bits != 8)) {
         set_status(QL_EINVAL);
         return nullptr;
     }

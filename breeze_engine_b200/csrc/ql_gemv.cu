@@ -4,12 +4,15 @@
 // tile_kernel, :320-365 tile_kernel8) from activations quantized by ql_quant.cu.
 //
 // Warp roles in a CTA that owns R row groups of 16 output features:
-//   * producer (1 warp, lane 0): streams stage i (BPS consecutive 32-wide
-//     blocks) into a STAGES-deep shared-memory ring with 1-D bulk copies
-//     (cp.async.bulk, no multicast): ONE copy per row group (its weight records
-//     -- weights, scales and zero points of BPS blocks are contiguous) plus ONE
-//     copy of the activation records shared by the CTA.  Bulk copies cost a
-//     roughly fixed number of cycles each, so stages are large and few.
+//   * producers (PROD warps, lane 0 each): producer p streams the stages
+//     i = p (mod PROD) (BPS consecutive 32-wide blocks each) into a
+//     STAGES-deep shared-memory ring with 1-D bulk copies (cp.async.bulk, no
+//     multicast): ONE copy per row group (its weight records -- weights,
+//     scales and zero points of BPS blocks are contiguous) plus ONE copy of the
+//     activation records shared by the CTA.  Bulk copies cost a roughly fixed
+//     number of cycles each, so stages are large and few; and one issuing
+//     thread's copies stream at most ~16-19 GB/s on B200 however deep the ring
+//     (measured), so CTAs that are few per SM use several producers.
 //   * consumers (S per row group): warp (r, s) takes stages i = s, s+S, ...  Per
 //     block: one 16x32 weight fragment (LDS.128 INT8; LDS.64 + 7 integer ops
 //     per 8 nibbles INT4); per 8-token group one LDS.128 of both activation
@@ -50,7 +53,7 @@ struct DecodeParams {
     int* err;
     int M, N, nblk, G, ldc;
     int TPB, TPBA, QREC;     // activation record geometry
-    int R, SPLIT, BPS, STAGES;
+    int R, SPLIT, BPS, STAGES, PROD;
     uint32_t stage_bytes;
     uint32_t off_Q;                        // activation records inside a stage
     uint32_t off_relay, off_stages;        // offsets inside dynamic shared memory
@@ -78,7 +81,7 @@ struct Chunk {
 };
 
 template <int BITS, bool HALF, bool ZP, int MT, bool HP, bool OUT_CS>
-__global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(384) decode_kernel(const DecodeParams p) {
     using Geo = Geom<BITS, HALF, ZP, HP>;
     constexpr int C = Chunk<MT>::C;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -108,9 +111,12 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
     // anything this grid reads or writes, and meanwhile prefetches its weights.
     pdl_launch_dependents();
 
-    if (warp == consumers) {
-        // ------------------------------------------------------------ producer
+    if (warp >= consumers) {
+        // ----------------------------------------------------------- producers
+        // producer pr issues the stages i = pr (mod PROD); STAGES is a multiple
+        // of PROD, so it waits only on ring slots it filled itself
         if (lane != 0) return;
+        const int pr = warp - consumers;
         auto issue = [&](int i, bool weights, bool acts) {
             const int s = i % p.STAGES;
             const uint32_t base = smem_u32(stages + static_cast<size_t>(s) * p.stage_bytes);
@@ -130,16 +136,17 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
                 bulk_g2s(base + p.off_Q, p.q + static_cast<size_t>(b0) * p.QREC, nb * p.QREC, full);
         };
         const int first = min(p.STAGES, nst);
-        for (int i = 0; i < first; ++i) issue(i, true, false);
+        for (int i = pr; i < first; i += p.PROD) issue(i, true, false);
         pdl_wait();                                   // activations come from the previous grid
-        for (int i = 0; i < first; ++i) issue(i, false, true);
-        for (int i = first; i < nst; ++i) {
+        for (int i = pr; i < first; i += p.PROD) issue(i, false, true);
+        for (int i = first + ((pr - first) % p.PROD + p.PROD) % p.PROD; i < nst; i += p.PROD) {
             const int s = i % p.STAGES;
             if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) {
-                // Giving up: let the copies already issued land before the CTA
-                // can exit (each slot's last issued phase; bounded waits).
-                for (int j = max(0, i - p.STAGES); j < i; ++j)
-                    if (!mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
+                // Giving up: let this producer's copies already issued land
+                // before the CTA can exit (each slot's last issued phase;
+                // bounded waits).
+                for (int j = i - p.STAGES; j < i; j += p.PROD)
+                    if (j >= 0 && !mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
                 return;
             }
             issue(i, true, true);
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__(288) decode_kernel(const DecodeParams p) {
 // ------------------------------------------------------------------ host side
 
 struct DecodeConfig {
-    int R, SPLIT, BPS, STAGES;
+    int R, SPLIT, BPS, STAGES, PROD;
 };
 
 static int g_num_sms = 0;
@@ -364,16 +371,25 @@ static DecodeConfig choose_config(int G, int nblk, int C, int rec, int qrec, int
     // row has enough blocks, stages of 2C blocks.  (Measured on B200 at M = 1:
     // 23-41% faster on 5120x6144, 6144x5120 and 17408x5120 layers.)
     const int max_warps = bits == 4 ? 4 : 8;
+    // Tuning override "R,SPLIT,BPS,STAGES[,PROD]" (each 0 = keep the planner's
+    // choice), applied where the planner makes that choice.  Values that break
+    // the planner's invariants are rejected by launch_t.
+    int ov_r = 0, ov_sp = 0, ov_b = 0, ov_s = 0, ov_p = 0;
+    if (const char* env = std::getenv("BREEZE_QL_DECODE_CONFIG"))
+        if (std::sscanf(env, "%d,%d,%d,%d,%d", &ov_r, &ov_sp, &ov_b, &ov_s, &ov_p) < 4)
+            ov_r = ov_sp = ov_b = ov_s = ov_p = 0;
     c.R = 1;
     c.SPLIT = 1;
     if (G >= 4 * g_num_sms) c.R = 4;
     else if (G >= 2 * g_num_sms) c.R = 2;
+    if (ov_r > 0) c.R = ov_r;
     while (c.R <= 2 && c.SPLIT < 8 && c.R * c.SPLIT < max_warps &&
            static_cast<long long>(G) * c.SPLIT * 2 <= target)
         c.SPLIT *= 2;
     const int nblk_even = (nblk + 1) & ~1;
     // A split stage is one or two sub-chunks (C blocks); at least two stages per split.
     while (c.SPLIT > 1 && (nblk_even + C - 1) / C < 2 * c.SPLIT) c.SPLIT /= 2;
+    if (ov_sp > 0) c.SPLIT = ov_sp;
     if (c.SPLIT > 1) {
         c.BPS = C;
         if (bits == 4 && (nblk_even + 2 * C - 1) / (2 * C) >= 2 * c.SPLIT) c.BPS = 2 * C;
@@ -386,24 +402,24 @@ static DecodeConfig choose_config(int G, int nblk, int C, int rec, int qrec, int
             c.BPS += C;
     }
     if (c.BPS > nblk_even) c.BPS = std::max(2, ((nblk_even + C - 1) / C) * C);
+    if (ov_b > 0) c.BPS = ov_b;
+    // One producer: on the INT8 decode sweep (B200, M = 1..16) two producers
+    // were within 1% and four 26% slower (their ring rounds up to a multiple
+    // of four stages); this kernel's 50 MB layers are not producer-bound.
+    c.PROD = 1;
+    if (ov_p > 0) c.PROD = ov_p;
+    // Ring slots go back to the warp (consumer and producer) that used them
+    // last: STAGES is a multiple of SPLIT and of PROD.
+    const int unit = std::max(c.SPLIT, c.PROD) % std::min(c.SPLIT, c.PROD) == 0 ? std::max(c.SPLIT, c.PROD)
+                                                                               : c.SPLIT * c.PROD;
     const int st = stage_bytes_for(c.R, c.BPS, rec, qrec);
-    // ~48 KB in flight per CTA, >= 2 stages per split, a multiple of SPLIT.
+    // ~48 KB in flight per CTA, >= 2 stages per split.
     c.STAGES = std::max(2 * c.SPLIT, (49152 + st - 1) / st);
     c.STAGES = std::min(c.STAGES, std::max(2 * c.SPLIT, 8));
-    c.STAGES = ((c.STAGES + c.SPLIT - 1) / c.SPLIT) * c.SPLIT;
+    c.STAGES = ((c.STAGES + unit - 1) / unit) * unit;
     if (c.STAGES < 2) c.STAGES = 2;
-    while (c.STAGES - c.SPLIT >= std::max(2, c.SPLIT) && c.STAGES * st > SMEM_BUDGET) c.STAGES -= c.SPLIT;
-    // Tuning override "R,SPLIT,BPS,STAGES" (each 0 = keep the planner's choice).
-    // Values that break the planner's invariants are rejected by launch_t.
-    if (const char* env = std::getenv("BREEZE_QL_DECODE_CONFIG")) {
-        int r = 0, sp = 0, b = 0, s = 0;
-        if (std::sscanf(env, "%d,%d,%d,%d", &r, &sp, &b, &s) == 4) {
-            if (r > 0) c.R = r;
-            if (sp > 0) c.SPLIT = sp;
-            if (b > 0) c.BPS = b;
-            if (s > 0) c.STAGES = s;
-        }
-    }
+    while (c.STAGES - unit >= std::max(2, c.SPLIT) && c.STAGES * st > SMEM_BUDGET) c.STAGES -= unit;
+    if (ov_s > 0) c.STAGES = ov_s;
     return c;
 }
 
@@ -416,6 +432,7 @@ static cudaError_t launch_t(const DecodeParams& p0, const DecodeConfig& c, cudaS
     p.SPLIT = c.SPLIT;
     p.BPS = c.BPS;
     p.STAGES = c.STAGES;
+    p.PROD = c.PROD;
     p.off_Q = c.R * c.BPS * Geo::REC;
     p.stage_bytes = stage_bytes_for(c.R, c.BPS, Geo::REC, p.QREC);
     const int NS = relay_slots(c.SPLIT);
@@ -428,7 +445,8 @@ static cudaError_t launch_t(const DecodeParams& p0, const DecodeConfig& c, cudaS
     // the kernel relies on (16-byte copies, slots owned by one warp).
     const int consumers = c.R * c.SPLIT;
     if (smem > 227 * 1024 || c.BPS < 2 || (c.BPS % C) || c.STAGES < 2 || c.R < 1 || c.R > 8 ||
-        c.SPLIT < 1 || c.SPLIT > 8 || consumers > 8 || (c.STAGES % c.SPLIT) || (p.QREC % 16) ||
+        c.SPLIT < 1 || c.SPLIT > 8 || consumers > 8 || (c.STAGES % c.SPLIT) || c.PROD < 1 || c.PROD > 4 ||
+        (c.STAGES % c.PROD) || (p.QREC % 16) ||
         (Geo::REC % 16) || (p.off_Q % 16))
         return cudaErrorInvalidConfiguration;
     auto kern = decode_kernel<BITS, HALF, ZP, MT, HP, OUT_CS>;
@@ -445,7 +463,7 @@ static cudaError_t launch_t(const DecodeParams& p0, const DecodeConfig& c, cudaS
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.G + c.R - 1) / c.R);
-    cfg.blockDim = dim3(32 * (consumers + 1));
+    cfg.blockDim = dim3(32 * (consumers + c.PROD));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -788,10 +788,8 @@ bool use_chain(const Weight* w) {
 // INT4 weights at one or two tokens run this file's kernels unless
 // BREEZE_QL_DECODE_DP4A=0.
 bool decode_dp4a_applies(const Weight* w, const ActView& act) {
-    static const int off = [] {
-        const char* v = std::getenv("BREEZE_QL_DECODE_DP4A");
-        return (v && v[0] == '0') ? 1 : 0;
-    }();
+    const char* v = std::getenv("BREEZE_QL_DECODE_DP4A");
+    const bool off = v && v[0] == '0';
     return !off && w->bits == 4 && act.MT == 1 && act.TPB >= 1 && act.TPB <= 2;
 }
 

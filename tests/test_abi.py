@@ -73,6 +73,7 @@ def test_native_rejects_bad_contract(N, K, bits, scale_bits):
     qw, sc, _ = fixture_weights(16, 32, 4, np.float32, False)
     lib = L.load()
     assert not lib.i4_prepack_onnx(qw.ctypes.data, sc.ctypes.data, None, N, K, bits, scale_bits)
+    assert lib.ql_last_status() == L.QL_EINVAL      # a bad contract, not an allocation failure
 
 
 def test_int8_with_zero_points_rejected_natively():

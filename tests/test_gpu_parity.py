@@ -382,3 +382,25 @@ def test_dp4a_chain_configs(cfg, N, oracle, monkeypatch):
     finally:
         qlc.free(h)
         qlc.set_hi_prec(False)
+
+
+@pytest.mark.parametrize("bits,half", [(8, False), (8, True), (4, True)])
+@pytest.mark.parametrize("cfg", ["0,0,0,0,2", "0,0,0,0,4", "4,1,0,0,4", "1,4,0,0,2", "2,2,0,0,4", "1,2,0,0,4"])
+def test_decode_kernel_producers(bits, half, cfg, oracle, monkeypatch):
+    """The tensor-core decode kernel with two or four producer warps (each
+    issuing every PROD-th stage of the ring) gives the same bits at 1, 5, 16
+    and 64 tokens, with and without a K split (partial last stages: 159
+    blocks)."""
+    N, K = 208, 5088
+    monkeypatch.setenv("BREEZE_QL_DECODE_CONFIG", cfg)
+    monkeypatch.setenv("BREEZE_QL_DECODE_DP4A", "0")
+    qw, sc, qz = _weights(N, K, bits, False, half, 11 + bits)
+    h = qlc.prepack(qw, sc, qz, N, K, bits)
+    qlc.set_hi_prec(True)
+    try:
+        for M in (1, 5, 16, 64):
+            a = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+            assert bits_equal(qlc.matmul_dev(h, a, N), oracle.matmul(qw, sc, qz, N, K, bits, a, hi_prec=True)), M
+    finally:
+        qlc.free(h)
+        qlc.set_hi_prec(False)
