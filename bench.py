@@ -17,8 +17,10 @@ Workloads (``--workload``):
   per second counted as the headline metric does: ``4*M*N*K`` per call (two
   INT8 passes of 2*M*N*K each).  The default ``decode`` line also carries this
   workload's measurement under ``secondary.prefill``, and configs[3]'s INT4
-  layer set at M = 1 under ``secondary.layer_m1`` (``--no-secondary`` skips
-  both), so one driver run measures both halves of the metric.
+  layer set at M = 1 under ``secondary.layer_m1``, and with ``--gpus P > 1``
+  configs[4]'s sharded layers under ``secondary.sharded_m1`` /
+  ``secondary.sharded_m2048`` (``--no-secondary`` skips them all), so one
+  driver run measures both halves of the metric.
 * ``mlp_front``: the front of a Qwen3.5-27B MLP block at decode batch sizes
   (M in {1, 4, 8, 16}; H = 5120, intermediate 17408, INT4 with fp16 scales):
   the RMSNorm fused into the activation quantizer, then one decode launch over
@@ -796,11 +798,15 @@ def run_ours(args):
     line = _measure(args, WORKLOADS[args.workload](), lib, rank, local_rank, world)
     # The headline metric names both halves of the path: the default decode
     # line also carries configs[2]'s prefill GEMM and configs[3]'s INT4 layer set
-    # at one token (the 27B-class decode shapes), measured the same way.
+    # at one token (the 27B-class decode shapes), measured the same way; on
+    # several GPUs also configs[4], the sharded layers at 1 and 2048 tokens.
     if args.workload == "decode" and not args.no_secondary:
         keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "e2e",
                 "cpu_baseline", "gpu_launches", "clocks")
-        for name, make in (("prefill", PrefillWorkload), ("layer_m1", lambda: LayerSetWorkload(1))):
+        extra = [("prefill", PrefillWorkload), ("layer_m1", lambda: LayerSetWorkload(1))]
+        if world > 1:
+            extra += [("sharded_m1", lambda: ShardedWorkload(1)), ("sharded_m2048", lambda: ShardedWorkload(2048))]
+        for name, make in extra:
             sec = _measure(args, make(), lib, rank, local_rank, world)
             if rank == 0:
                 line.setdefault("secondary", {})[name] = {k: sec[k] for k in keep if k in sec}
@@ -1026,6 +1032,8 @@ def _measure(args, wl, lib, rank, local_rank, world):
         if world > 1 and any(layer.mode == "col" for layer, _, _ in calls):
             cfg["exchange"] = ("one-shot peer-memory all-gather (ql_peer_allgather_cols_dev)"
                                if exchange is not None else "NCCL all_gather_into_tensor")
+            if exchange is not None and "parallelism" in cfg:
+                cfg["parallelism"] = cfg["parallelism"].replace("NCCL all-gather", "peer-memory all-gather")
         line = {
             "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "impl": "ours", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
