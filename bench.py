@@ -34,8 +34,10 @@ With ``--gpus P`` (total work fixed, "strong" scaling) the decode sweep
 column-shards the LM head (N/P per GPU, NCCL all-gather of the output; or the
 library's peer-memory all-gather with ``--exchange peer``) and deals the calls
 of the two 50 MB layers round-robin over the GPUs as whole, independent calls;
-``prefill`` column-shards its layer; ``sharded_m1`` / ``sharded_m2048``
-(configs[4]) shard one layer column-parallel and one row-parallel.  Every
+``sharded_m1`` / ``sharded_m2048`` shard one layer column-parallel
+and one row-parallel.  Layers that are not large -- ``prefill``'s 44.6 MB and
+the 3-50 MB projections of ``layer_m1`` / ``layer_m512`` -- run whole on every
+GPU, each rank on its own inputs (replicas, "weak" scaling, no collective).  Every
 other config is also a parity-test case (tests/).
 
 Inputs stay resident in HBM; every call streams its weights from HBM because
@@ -197,14 +199,16 @@ class Layer:
     ``mode='col'``: rank r keeps output rows [r N/P, (r+1) N/P) (column-parallel);
     ``mode='row'``: rank r keeps input blocks [r K/P, (r+1) K/P) (row-parallel);
     ``mode='whole'``: the full layer, packed only where ``build`` is true (the
-    ranks that run one of its calls)."""
+    ranks that run one of its calls);
+    ``mode='replica'``: the full layer on every rank, which runs its own calls
+    (independent token streams, no collective)."""
 
     def __init__(self, lib, K, N, bits, world, rank, seed, copies, mode="col", build=True):
         import torch
         from breeze_engine_b200 import backend
         from breeze_engine_b200.quant import quantize_matmul_nbits_torch
         self.K, self.N, self.bits, self.mode = K, N, bits, mode
-        if mode == "whole":
+        if mode in ("whole", "replica"):
             world, rank = 1, 0
         self.n_local = N // world if mode != "row" else N
         self.k_local = K if mode != "row" else K // world
@@ -369,8 +373,13 @@ class PrefillWorkload:
     K, N, Ms, bits = 5120, 17408, [128, 512, 2048], 4
     kernel = "gemmw_kernel (ql_gemmw.cu, tcgen05 kind::f16 on per-call FP16-dequantized weights)"
 
+    # A 44.6 MB weight is not a large layer: on several GPUs every rank runs the
+    # whole layer on its own token batch (no collective; weak scaling).
+    replicas = True
+
     def build(self, lib, world, rank):
-        layer = Layer(lib, self.K, self.N, self.bits, world, rank, 3000, len(self.Ms))
+        layer = Layer(lib, self.K, self.N, self.bits, world, rank, 3000, len(self.Ms),
+                      mode="replica" if world > 1 else "col")
         acts = self.make_acts("cuda")
         calls = [(layer, layer.handles[j % len(layer.handles)], M) for j, M in enumerate(self.Ms)]
         return [layer], acts, calls
@@ -418,7 +427,7 @@ class PrefillWorkload:
                 "activations": "two-pass INT16 (hi_prec=1); N(0,1), 1% channels x20",
                 "l2": "3 rotated weight copies; step working set > L2",
                 "timing": "CUDA graph of one step (3 quantize+GEMM calls), CUDA events",
-                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+                "parallelism": "1 GPU" if world == 1 else f"replicas on {world} GPUs (no collective)"}
 
     def cpu_calls(self):
         return [(self.K, self.N, self.bits, [128], 3000)]
@@ -468,10 +477,14 @@ class LayerSetWorkload(_OpsOrBytes):
         self.metric = (f"27B-class layer projection set, M={M}: "
                        + ("HBM throughput" if self.unit == "GB/s" else "INT8 TOPS (4*M*N*K per call)"))
 
+    # The projections (3-50 MB) are not large layers: on several GPUs every rank
+    # runs the whole sequence on its own tokens (no collective; weak scaling).
+    replicas = True
+
     def build(self, lib, world, rank):
-        total = sum(K * N // 2 for _, K, N in self.shapes) // world
+        total = sum(K * N // 2 for _, K, N in self.shapes)
         copies = int(min(4, max(1, -(-2 * L2_BYTES // total))))
-        layers = [Layer(lib, K, N, self.bits, world, rank, 4000 + i, copies)
+        layers = [Layer(lib, K, N, self.bits, world, rank, 4000 + i, copies, mode="replica" if world > 1 else "col")
                   for i, (_, K, N) in enumerate(self.shapes)]
         acts = {(self.M, K): _outlier_acts(self.M, K, 21 + K) for K in sorted({K for _, K, _ in self.shapes})}
         calls = [(layer, layer.handles[0], self.M) for layer in layers]
@@ -485,7 +498,7 @@ class LayerSetWorkload(_OpsOrBytes):
                 "activations": "two-pass INT16 (hi_prec=1); N(0,1), 1% channels x20",
                 "l2": "7-call step touches > L2 (192 MB of weights)",
                 "timing": "CUDA graph of one step (7 quantize+matmul calls), CUDA events",
-                "parallelism": f"column-parallel N/{world}" + (" + NCCL all-gather" if world > 1 else "")}
+                "parallelism": "1 GPU" if world == 1 else f"replicas on {world} GPUs (no collective)"}
 
     def host_acts(self):
         dev = _gen_device()
@@ -849,7 +862,7 @@ def _measure(args, wl, lib, rank, local_rank, world):
         if (layer.k_local, M) not in wss or wss[(layer.k_local, M)].numel() < need:
             wss[(layer.k_local, M)] = torch.empty(need, dtype=torch.uint8, device="cuda")
         # row-parallel: this rank's contiguous K slice of the activations
-        local_a[(id(layer), M)] = (acts[(M, layer.K)] if layer.mode == "col" else
+        local_a[(id(layer), M)] = (acts[(M, layer.K)] if layer.mode != "row" else
                                    torch.empty((M, layer.k_local), dtype=torch.float32, device="cuda"))
 
     def step():
@@ -928,6 +941,9 @@ def _measure(args, wl, lib, rank, local_rank, world):
     clock_info["window"] = "sampled over ~1 s of back-to-back steps plus the timed region"
 
     step_amount = wl.step_amount(calls)
+    replicas = world > 1 and getattr(wl, "replicas", False)
+    if replicas:
+        step_amount *= world                  # every rank ran the whole step on its own inputs
     value = wl.value(step_amount * args.steps, t)
 
     # ---- per-launch pass (roofline): the matmul kernel alone, on activations
@@ -1037,7 +1053,7 @@ def _measure(args, wl, lib, rank, local_rank, world):
         line = {
             "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "impl": "ours", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak" if replicas else "strong", "vs_baseline": None,
             "dtype": "s8xs8/u8->s32, f32 rescale",
             "data": DATA,
             "config": cfg,

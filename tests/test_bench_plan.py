@@ -1,11 +1,14 @@
 """Host-side checks of bench.py's multi-GPU plans (no GPU needed).
 
 The driver runs `bench.py --gpus N` for N = 1, 2, 4, 8 with the default
-decode workload.  At N > 1 only the LM head is column-sharded (NCCL
-all-gather); the 50 MB layers stay whole and their calls are dealt to the
-GPUs.  These tests pin that plan and the divisibility every sharded workload
-needs at each N (output rows in whole 16-row groups per GPU, input blocks of 32
-in equal shares for row-parallel layers).
+decode workload.  At N > 1 only large layers are sharded: the LM head
+column-parallel (all-gather), configs[4]'s layers column- and row-parallel;
+the decode sweep's 50 MB layers stay whole and their calls are dealt to the
+GPUs; the prefill layer and the 27B-class layer set run as replicas (every
+rank the whole layer on its own inputs, no collective).  These tests pin those
+plans and the divisibility every sharded workload needs at each N (output
+rows in whole 16-row groups per GPU, input blocks of 32 in equal shares for
+row-parallel layers).
 """
 import collections
 
@@ -39,14 +42,28 @@ def test_decode_plan(world):
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_sharded_shapes_divide(world):
-    """Every layer the other workloads column-shard (prefill, the 27B-class
-    layer set, configs[4]'s column-parallel layer) splits into whole 16-row
-    groups, and configs[4]'s row-parallel layer into whole 32-wide blocks."""
-    col = [(bench.PrefillWorkload.K, bench.PrefillWorkload.N), (8192, 65536)]
-    col += [(K, N) for _, K, N in bench.LayerSetWorkload.shapes]
-    for K, N in col:
-        assert N % (16 * world) == 0, (K, N, world)
+    """configs[4]'s column-parallel layer splits into whole 16-row groups and
+    its row-parallel layer into whole 32-wide blocks at every N."""
+    assert 65536 % (16 * world) == 0
     assert (65536 // 32) % world == 0
+
+
+def test_small_layer_workloads_are_replicas():
+    """Layers that are not large run whole on every rank at N > 1: the prefill
+    layer and the layer set are replicas; the decode sweep and configs[4]
+    shard."""
+    assert bench.PrefillWorkload.replicas and bench.LayerSetWorkload.replicas
+    assert not getattr(bench.DecodeWorkload, "replicas", False)
+    assert not getattr(bench.ShardedWorkload, "replicas", False)
+
+
+@pytest.mark.parametrize("mode,n_local,k_local", [("col", 4352, 5120), ("row", 17408, 1280),
+                                                  ("whole", 17408, 5120), ("replica", 17408, 5120)])
+def test_layer_geometry_per_mode(mode, n_local, k_local):
+    """Rank 2 of 4: its slice of a 5120 x 17408 layer in each mode (no packing)."""
+    layer = bench.Layer(None, 5120, 17408, 4, 4, 2, 0, 1, mode=mode, build=False)
+    assert (layer.n_local, layer.k_local) == (n_local, k_local)
+    assert layer.k0 == (2 * 1280 if mode == "row" else 0)
 
 
 def test_mlp_front_workload_streams_from_hbm():
