@@ -31,9 +31,12 @@ Workloads (``--workload``):
   replicas.
 
 With ``--gpus P`` (total work fixed, "strong" scaling) the decode sweep
-column-shards the LM head (N/P per GPU, NCCL all-gather of the output; or the
-library's peer-memory all-gather with ``--exchange peer``) and deals the calls
-of the two 50 MB layers round-robin over the GPUs as whole, independent calls;
+column-shards the LM head (N/P per GPU; the output is all-gathered by the
+library's one-shot peer-memory exchange, or by NCCL with ``--exchange nccl``)
+and deals the calls of the two 50 MB layers round-robin over the GPUs as
+whole, independent calls.  The calls of a step are independent, so each call's
+collective runs on a second stream while the next call's matmul runs
+(``--no-overlap`` serialises them);
 ``sharded_m1`` / ``sharded_m2048`` shard one layer column-parallel
 and one row-parallel.  Layers that are not large -- ``prefill``'s 44.6 MB and
 the 3-50 MB projections of ``layer_m1`` / ``layer_m512`` -- run whole on every
@@ -269,7 +272,7 @@ class DecodeWorkload:
     kernel = "decode_kernel (ql_gemv.cu)"
 
     # Layers of at least this many weight bytes are column-sharded across the
-    # GPUs (NCCL all-gather of the outputs); smaller layers stay whole and their
+    # GPUs (all-gather of the outputs); smaller layers stay whole and their
     # calls -- independent units of the sweep -- are dealt round-robin to the
     # GPUs, so only sharded shapes have a collective.
     SHARD_BYTES = 256 << 20
@@ -814,7 +817,7 @@ def run_ours(args):
     # at one token (the 27B-class decode shapes), measured the same way; on
     # several GPUs also configs[4], the sharded layers at 1 and 2048 tokens.
     if args.workload == "decode" and not args.no_secondary:
-        keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "e2e",
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "scaling", "config", "roofline", "e2e",
                 "cpu_baseline", "gpu_launches", "clocks")
         extra = [("prefill", PrefillWorkload), ("layer_m1", lambda: LayerSetWorkload(1))]
         if world > 1:
@@ -842,7 +845,7 @@ def _measure(args, wl, lib, rank, local_rank, world):
     layers, acts, calls = wl.build(lib, world, rank)
     owners = getattr(wl, "owners", {})
     exchange = None
-    if world > 1 and args.exchange == "peer":
+    if world > 1 and args.exchange == "peer" and any(layer.mode == "col" for layer, _, _ in calls):
         # one peer-memory exchange sized for the largest column-parallel output
         from breeze_engine_b200.sharded import PeerExchange
         cap = max([4 * M * layer.N for layer, _, M in calls if layer.mode == "col"] or [16])
@@ -865,8 +868,24 @@ def _measure(args, wl, lib, rank, local_rank, world):
         local_a[(id(layer), M)] = (acts[(M, layer.K)] if layer.mode != "row" else
                                    torch.empty((M, layer.k_local), dtype=torch.float32, device="cuda"))
 
+    # The calls of a step are independent units: with overlap, each call's
+    # collective runs on a second stream while the next call's matmul runs,
+    # and the step ends only when every collective has (the stream joins back).
+    comm = torch.cuda.Stream() if world > 1 and not args.no_overlap else None
+
+    def collective(layer, c):
+        if layer.mode == "col":
+            if exchange is not None:
+                exchange.gather(c)
+            else:
+                gather_columns(c)
+        elif layer.mode == "row":
+            reduce_partials(c, "scatter")
+
     def step():
-        s_ptr = torch.cuda.current_stream().cuda_stream
+        main = torch.cuda.current_stream()
+        s_ptr = main.cuda_stream
+        forked = False
         for layer, h, M in calls:
             if not mine(layer, M):
                 continue
@@ -877,14 +896,18 @@ def _measure(args, wl, lib, rank, local_rank, world):
                                       ws.data_ptr(), ws.numel(), s_ptr)
             if rc:
                 raise RuntimeError(f"ql_matmul_dev_ws failed: {rc}")
-            if world > 1:
-                if layer.mode == "col":
-                    if exchange is not None:
-                        exchange.gather(c)
-                    else:
-                        gather_columns(c)
-                elif layer.mode == "row":
-                    reduce_partials(c, "scatter")
+            if world > 1 and layer.mode in ("col", "row"):
+                if comm is None:
+                    collective(layer, c)
+                else:
+                    done = torch.cuda.Event()
+                    done.record(main)
+                    comm.wait_event(done)
+                    with torch.cuda.stream(comm):
+                        collective(layer, c)
+                    forked = True
+        if forked:                            # join only a stream this step forked
+            main.wait_stream(comm)
 
     def barrier():
         if world > 1:
@@ -1048,6 +1071,8 @@ def _measure(args, wl, lib, rank, local_rank, world):
         if world > 1 and any(layer.mode == "col" for layer, _, _ in calls):
             cfg["exchange"] = ("one-shot peer-memory all-gather (ql_peer_allgather_cols_dev)"
                                if exchange is not None else "NCCL all_gather_into_tensor")
+            cfg["overlap"] = ("each call's collective on a second stream, overlapping the next call"
+                              if comm is not None else "none")
             if exchange is not None and "parallelism" in cfg:
                 cfg["parallelism"] = cfg["parallelism"].replace("NCCL all-gather", "peer-memory all-gather")
         line = {
@@ -1351,9 +1376,12 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="peer",
                     help="column-parallel output exchange at N > 1: NCCL all-gather, or the one-shot "
                          "peer-memory all-gather of this library (ql_peer_allgather_cols_dev)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="at N > 1, run each call's collective after it on the same stream instead of "
+                         "overlapping it with the next (independent) call")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
