@@ -47,6 +47,7 @@ struct DeviceState {
     cudaStream_t copy_stream = nullptr;   // i4_matmul: output copies overlapping the matmul
     cudaEvent_t chunk_done[8] = {};       // i4_matmul: one per output column chunk
     int* host_err = nullptr;              // pinned copy of the device error word (i4_matmul)
+    cudaEvent_t copies_done = nullptr;    // i4_matmul: the output copies joined back into the call's stream
 };
 DeviceState g_dev[MAX_DEVICES];
 
@@ -949,8 +950,10 @@ QL_API int ql_quantize_dev(const float* dA, int M, int K, uint8_t* dHi, uint8_t*
 // C[M,N] fp32 out, synchronous.  Like the reference it returns nothing; a
 // failure leaves C untouched and is reported by ql_last_status().
 // Output columns per chunk of the synchronous host-pointer call: outputs of at
-// least 2 chunks x 512 KB are split into up to 8 column chunks (multiples of
-// 128 columns, so every chunk is whole GEMM tiles and decode row groups); each
+// least 2 MB are split into one column chunk per MB, up to 8 (measured on B200,
+// LM head 4096 x 151936 INT8 through i4_matmul: 2 MB at M = 4 -> 2 chunks 187 us,
+// 4.9 MB at M = 8 -> 4 chunks 202 us against 213 with 8, 9.7 MB at M = 16 -> 8
+// chunks 266 us against 360 with one), in multiples of 128 columns, so every chunk is whole GEMM tiles and decode row groups); each
 // chunk's matmul runs on the call's stream and its device -> host copy starts
 // on a second stream as soon as it is done, overlapping the next chunk.
 // After a synchronous call: a bounded wait of one of its kernels gave up if the
@@ -966,9 +969,66 @@ static int take_device_error(DeviceState* st, int* err_word, cudaStream_t s) {
 
 static int output_chunks(int M, int N) {
     const size_t bytes = static_cast<size_t>(M) * N * 4;
-    int chunks = static_cast<int>(std::min<size_t>(8, bytes / (512 * 1024)));
+    int chunks = static_cast<int>(std::min<size_t>(8, bytes / (1024 * 1024)));
+    if (const char* v = std::getenv("BREEZE_QL_OUTPUT_CHUNKS")) {      // tuning override (0: planner)
+        const int c = std::atoi(v);
+        if (c > 0) chunks = std::min(c, 8);
+    }
     while (chunks > 1 && N / chunks < 128) --chunks;
     return std::max(1, chunks);
+}
+
+// Enqueues one host-pointer call on s (and the copy stream, joined back into
+// s): copy A in, quantize and multiply (in output column chunks whose copies
+// overlap the next chunk), copy C and the device error word out.  Nothing
+// here synchronises; the caller drains both streams.
+static int enqueue_host_call(const Weight* w, const float* A, int M, float* C, DeviceState* st, cudaStream_t s,
+                             bool hp, float* dA, float* dC, void* ws, size_t ws_bytes, int* err_word) {
+    cudaError_t e = cudaMemcpyAsync(dA, A, static_cast<size_t>(M) * w->K * 4, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_status(e);
+    const int chunks = output_chunks(M, w->N);
+    if (chunks == 1) {
+        int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
+        if (rc != QL_OK) return rc;
+        e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && err_word)
+            e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
+        return cuda_status(e);
+    }
+    const bool fp16_ops = gemmw_applies(w, M);      // the workspace was sized for it
+    uint8_t* wbase = static_cast<uint8_t*>(ws);
+    int rc = fp16_ops ? run_gemmw_prep(w, dA, M, wbase, s, hp) : run_quantize(dA, M, w->K, ws, s, hp);
+    if (rc != QL_OK) return rc;
+    // column chunks of whole 128-column tiles; the last takes the remainder
+    const int per = ((w->N / chunks) / 128) * 128;
+    for (int i = 0; i < chunks && e == cudaSuccess; ++i) {
+        const int n0 = i * per;
+        const int nc = (i == chunks - 1) ? w->N - n0 : per;
+        Weight view = *w;                         // rows n0 .. n0+nc of the same records
+        view.N = nc;
+        view.G = nc / 16;
+        view.W = w->W + static_cast<size_t>(n0 / 16) * w->nblk * w->REC;
+        if (fp16_ops) {
+            const uint8_t* wd = wbase + gemmw_act_region(M, w->nblk) + static_cast<size_t>(n0 / 128) * w->nblk * WREC16;
+            rc = cuda_status(launch_gemmw(&view, wd, wbase, M, hp, dC + n0, w->N, nullptr, s));
+        } else {
+            rc = run_compute(&view, ws, M, dC + n0, nullptr, s, hp, /*pdl=*/i == 0, /*ldc=*/w->N);
+        }
+        if (rc != QL_OK) break;
+        e = cudaEventRecord(st->chunk_done[i], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st->copy_stream, st->chunk_done[i], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(C + n0, static_cast<size_t>(w->N) * 4, dC + n0, static_cast<size_t>(w->N) * 4,
+                                  static_cast<size_t>(nc) * 4, M, cudaMemcpyDeviceToHost, st->copy_stream);
+    }
+    // the copy stream joins back into s (also after a failure, so a capture ends cleanly)
+    cudaError_t ej = cudaEventRecord(st->copies_done, st->copy_stream);
+    if (ej == cudaSuccess) ej = cudaStreamWaitEvent(s, st->copies_done, 0);
+    if (rc != QL_OK) return rc;
+    if (e == cudaSuccess) e = ej;
+    if (e == cudaSuccess && err_word)
+        e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
+    return cuda_status(e);
 }
 
 QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
@@ -1001,11 +1061,6 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
     float* dA = static_cast<float*>(st->buf);
     float* dC = reinterpret_cast<float*>(static_cast<uint8_t*>(st->buf) + a_bytes);
     void* ws = static_cast<uint8_t*>(st->buf) + a_bytes + c_bytes;
-    e = cudaMemcpyAsync(dA, A, static_cast<size_t>(M) * w->K * 4, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) {
-        cuda_status(e);
-        return;
-    }
     int* err_word = device_error_word();
     if (!st->host_err) {
         e = cudaHostAlloc(reinterpret_cast<void**>(&st->host_err), sizeof(int), cudaHostAllocDefault);
@@ -1015,61 +1070,24 @@ QL_API void i4_matmul(void* handle, const float* A, int M, float* C) {
             return;
         }
     }
-    *st->host_err = 0;
-    const int chunks = output_chunks(M, w->N);
-    if (chunks == 1) {
-        int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);
-        if (rc != QL_OK) return;
-        e = cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * w->N * 4, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess && err_word)
-            e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-        if (e == cudaSuccess) take_device_error(st, err_word, s);
-        else cuda_status(e);
-        return;
-    }
     if (!st->copy_stream) {
         e = cudaStreamCreateWithFlags(&st->copy_stream, cudaStreamNonBlocking);
         for (int i = 0; i < 8 && e == cudaSuccess; ++i)
             e = cudaEventCreateWithFlags(&st->chunk_done[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&st->copies_done, cudaEventDisableTiming);
         if (e != cudaSuccess) {
             cuda_status(e);
             return;
         }
     }
-    const bool fp16_ops = gemmw_applies(w, M);      // the workspace was sized for it above
-    uint8_t* wbase = static_cast<uint8_t*>(ws);
-    int rc = fp16_ops ? run_gemmw_prep(w, dA, M, wbase, s, hp) : run_quantize(dA, M, w->K, ws, s, hp);
-    if (rc != QL_OK) return;
-    // column chunks of whole 128-column tiles; the last takes the remainder
-    const int per = ((w->N / chunks) / 128) * 128;
-    for (int i = 0; i < chunks && e == cudaSuccess; ++i) {
-        const int n0 = i * per;
-        const int nc = (i == chunks - 1) ? w->N - n0 : per;
-        Weight view = *w;                         // rows n0 .. n0+nc of the same records
-        view.N = nc;
-        view.G = nc / 16;
-        view.W = w->W + static_cast<size_t>(n0 / 16) * w->nblk * w->REC;
-        if (fp16_ops) {
-            const uint8_t* wd = wbase + gemmw_act_region(M, w->nblk) + static_cast<size_t>(n0 / 128) * w->nblk * WREC16;
-            rc = cuda_status(launch_gemmw(&view, wd, wbase, M, hp, dC + n0, w->N, nullptr, s));
-        } else {
-            rc = run_compute(&view, ws, M, dC + n0, nullptr, s, hp, /*pdl=*/i == 0, /*ldc=*/w->N);
-        }
-        if (rc != QL_OK) break;
-        e = cudaEventRecord(st->chunk_done[i], s);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(st->copy_stream, st->chunk_done[i], 0);
-        if (e == cudaSuccess)
-            e = cudaMemcpy2DAsync(C + n0, static_cast<size_t>(w->N) * 4, dC + n0, static_cast<size_t>(w->N) * 4,
-                                  static_cast<size_t>(nc) * 4, M, cudaMemcpyDeviceToHost, st->copy_stream);
-    }
-    if (e == cudaSuccess && rc == QL_OK && err_word)
-        e = cudaMemcpyAsync(st->host_err, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
+    *st->host_err = 0;
+
+    const int rc = enqueue_host_call(w, A, M, C, st, s, hp, dA, dC, ws, ws_bytes, err_word);
     // both streams drain before returning (also after a failure, so no copy is in flight)
-    cudaError_t e1 = cudaStreamSynchronize(s);
-    cudaError_t e2 = cudaStreamSynchronize(st->copy_stream);
+    const cudaError_t e1 = cudaStreamSynchronize(s);
+    const cudaError_t e2 = cudaStreamSynchronize(st->copy_stream);
     if (rc != QL_OK) return;
-    if (e == cudaSuccess) e = (e1 != cudaSuccess) ? e1 : e2;
+    e = (e1 != cudaSuccess) ? e1 : e2;
     if (e == cudaSuccess) take_device_error(st, err_word, s);
     else cuda_status(e);
 }

@@ -526,8 +526,6 @@ int* device_error_word();   // ql_api.cu
 
 namespace {
 
-constexpr int D4_SMEM_BUDGET = 110 * 1024;   // dynamic shared memory per CTA: >= 2 CTAs per SM
-
 struct D4Config {
     int Q4, SPLIT, BPS, STAGES;
 };
