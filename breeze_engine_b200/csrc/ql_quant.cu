@@ -11,8 +11,11 @@
 // to int: NaN / inf / |x| >= 2^63 give 0, |x| in [2^31, 2^63) keep the low
 // 32 bits.  to_int_like_lrint() reproduces that for every float.
 //
-// One thread owns one (token, block) pair: it reads 128 contiguous bytes of A
-// and writes 16-byte chunks of each plane, so the kernel is a single HBM pass.
+// Decode layout: 8 lanes own one (token, block) pair, each reading 16 bytes of
+// A and writing one word of each plane (ql_quant.cuh, act_store_quad), so a
+// decode call waits for one short pass.  GEMM layout: one thread per pair,
+// 128 contiguous bytes of A in, 16-byte chunks of each plane out.  Both are a
+// single HBM pass.
 #include "ql_common.cuh"
 #include "ql_internal.h"
 #include "ql_quant.cuh"
@@ -28,18 +31,17 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const float* __restri
     // launched with PDL too): wait for it before reading A or writing planes.
     pdl_launch_dependents();
     pdl_wait();
+    // 8 lanes per (token, block) pair (ql_quant.cuh, act_store_quad); padded
+    // token rows quantize zeros into the zero record
     const int nblk = K / BLOCK_K;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<long long>(out.TPBA) * nblk) return;
-    const int m = static_cast<int>(idx / nblk);
-    const int b = static_cast<int>(idx % nblk);
-    if (m >= M) {   // padded token rows
-        act_zero_block<HP>(out, m, b);
-        return;
-    }
-    float v[32];
-    load_block<PRO>(A, lda, m, b, nrm, v);
-    act_store_block<HP>(v, out, m, b);
+    const long long unit = idx >> 3;
+    const int c = static_cast<int>(idx & 7);
+    const bool valid = unit < static_cast<long long>(out.TPBA) * nblk;
+    const int m = valid ? static_cast<int>(unit / nblk) : 0;
+    const int b = valid ? static_cast<int>(unit % nblk) : 0;
+    const float4 v = (valid && m < M) ? load_quad<PRO>(A, lda, m, b, c, nrm) : make_float4(0.f, 0.f, 0.f, 0.f);
+    act_store_quad<HP>(v, out, m, b, c, valid);
 }
 
 // GEMM-layout variant (M > 64, ql_gemm16.cu / ql_gemm.cu): the token-half-major
@@ -202,7 +204,7 @@ ActView act_carve(void* ws, int M, int nblk, bool hi_prec) {
 
 cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_prec,
                                 const ActView& out, cudaStream_t stream, const NormArgs* norm) {
-    const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
+    const long long total = 8LL * out.TPBA * (K / BLOCK_K);          // 8 lanes per (token, block)
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     const NormArgs n = norm ? *norm : NormArgs{};
@@ -219,7 +221,7 @@ cudaError_t launch_quantize_act(const float* A, int lda, int M, int K, bool hi_p
 // receives the values quantized.
 cudaError_t launch_quantize_act_silu(const float* G, const float* U, int ld, int M, int K, bool hi_prec,
                                      const ActView& out, float* dOut, cudaStream_t stream) {
-    const long long total = static_cast<long long>(out.TPBA) * (K / BLOCK_K);
+    const long long total = 8LL * out.TPBA * (K / BLOCK_K);          // 8 lanes per (token, block)
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     const NormArgs n{nullptr, nullptr, dOut, K, U, ld};

@@ -210,4 +210,95 @@ __device__ __forceinline__ void act_store_block(const float (&v)[32], const ActV
     }
 }
 
+// ---------------------------------------------------------------- 8 lanes per block
+// The decode-layout quantizer with one (token, block) pair per 8 consecutive
+// lanes: lane c of the group holds values 4c..4c+3 of the block.  The block's
+// amax (a maximum: exact in any order, NaN never wins the compare) and its sum
+// of quantized values (integers) are combined with xor-shuffles inside the
+// group; scale, inverse and every value's rounding are the same operations as
+// act_store_block, so the record is bit-identical -- at an eighth of the
+// serial latency per block, which is what a decode call waits for.  Every lane
+// of the warp must call these (shuffles), valid or not.
+
+// The 4 values (token m, block b, lane c) of the block, with the prologue.
+template <int PRO>
+__device__ __forceinline__ float4 load_quad(const float* __restrict__ A, int lda, int m, int b, int c,
+                                            const NormArgs& nrm) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + b * BLOCK_K) + c);
+    if (PRO == PRO_NORM) {
+        const float r = __ldg(nrm.row_inv + m);
+        const float4 g = __ldg(reinterpret_cast<const float4*>(nrm.w + b * BLOCK_K) + c);
+        v.x = __fmul_rn(__fmul_rn(v.x, r), g.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, r), g.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, r), g.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, r), g.w);
+    }
+    if (PRO == PRO_SILU) {
+        const float4 u = __ldg(reinterpret_cast<const float4*>(nrm.up + static_cast<size_t>(m) * nrm.ldu + b * BLOCK_K) + c);
+        v.x = silu_mul_ref(v.x, u.x);
+        v.y = silu_mul_ref(v.y, u.y);
+        v.z = silu_mul_ref(v.z, u.z);
+        v.w = silu_mul_ref(v.w, u.w);
+    }
+    if (PRO != PRO_NONE && nrm.hn)
+        reinterpret_cast<float4*>(nrm.hn + static_cast<size_t>(m) * nrm.ldh + b * BLOCK_K)[c] = v;
+    return v;
+}
+
+// Quantizes the group's block into its record; `store` false: take part in
+// the shuffles only.  Padded token rows pass zeros and get the zero record.
+template <bool HP>
+__device__ __forceinline__ void act_store_quad(float4 v, const ActView& out, int m, int b, int c, bool store) {
+    constexpr int LB = HP ? 16 : 8;
+    constexpr float QMAX = HP ? 32767.0f : 127.0f;
+    constexpr int IMAX = HP ? 32767 : 127;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float a = fabsf(vv[j]);
+        amax = (a > amax) ? a : amax;
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        const float a = __shfl_xor_sync(0xffffffffu, amax, o);
+        amax = (a > amax) ? a : amax;
+    }
+    const float scale = __fdiv_rn(amax, QMAX);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    uint32_t hword = 0, lword = 0;
+    int qsum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        int q = to_int_like_lrint(__fmul_rn(vv[j], inv));
+        q = q > IMAX ? IMAX : (q < -IMAX ? -IMAX : q);
+        qsum += q;
+        if (HP) {
+            const uint32_t u = static_cast<uint32_t>(q + 32768);
+            hword |= ((u >> 8) ^ 0x80u) << (8 * j);      // hi - 128 as a signed byte
+            lword |= (u & 0xFFu) << (8 * j);
+        } else {
+            lword |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);   // q8 as a signed byte
+        }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+    if (!store) return;
+    uint8_t* rec = out.q + static_cast<size_t>(b) * out.QREC;
+    if (m < out.TPB) {
+        // word c of each plane: slot t = c % 4, first (c < 4) or second half of the slot's words
+        uint8_t* slot = rec + m * 4 * LB + (c & 3) * LB + (c < 4 ? 0 : 4);
+        if (HP) {
+            *reinterpret_cast<uint32_t*>(slot) = hword;
+            *reinterpret_cast<uint32_t*>(slot + 8) = lword;
+        } else {
+            *reinterpret_cast<uint32_t*>(slot) = lword;
+        }
+    }
+    if (c == 0) {
+        reinterpret_cast<float*>(rec + out.TPB * 4 * LB)[m] = scale;
+        reinterpret_cast<int32_t*>(rec + out.TPB * 4 * LB + out.TPBA * 4)[m] = qsum;
+    }
+}
+
 }  // namespace ql
