@@ -111,16 +111,25 @@ __global__ void __launch_bounds__(NORM_THREADS) quantize_act_norm_kernel(const f
     pdl_wait();
     const int m = blockIdx.x;
     const int nblk = K / BLOCK_K;
-    if (m >= M) {
-        for (int b = threadIdx.x; b < nblk; b += NORM_THREADS) act_zero_block<HP>(out, m, b);
-        return;
-    }
-    const float r = block_row_inv(X + static_cast<size_t>(m) * ldx, K, eps);
-    for (int b = threadIdx.x; b < nblk; b += NORM_THREADS) {
-        float v[32];
-        load_raw_block(X, ldx, m, b, v);
-        norm_block(v, r, nrm, m, b);
-        act_store_block<HP>(v, out, m, b);
+    const bool real = m < M;                       // padded rows quantize zeros into zero records
+    const float r = real ? block_row_inv(X + static_cast<size_t>(m) * ldx, K, eps) : 0.0f;
+    // 8 lanes per block (ql_quant.cuh, act_store_quad); every lane runs every
+    // round so the group shuffles stay converged
+    const int c = threadIdx.x & 7;
+    for (int b0 = 0; b0 < nblk; b0 += NORM_THREADS / 8) {
+        const int b = b0 + (threadIdx.x >> 3);
+        const bool valid = b < nblk;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid && real) {
+            v = __ldg(reinterpret_cast<const float4*>(X + static_cast<size_t>(m) * ldx + b * BLOCK_K) + c);
+            const float4 g = __ldg(reinterpret_cast<const float4*>(nrm.w + b * BLOCK_K) + c);
+            v.x = __fmul_rn(__fmul_rn(v.x, r), g.x);    // (x * inv) * w, each product rounded
+            v.y = __fmul_rn(__fmul_rn(v.y, r), g.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, r), g.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, r), g.w);
+            if (nrm.hn) reinterpret_cast<float4*>(nrm.hn + static_cast<size_t>(m) * nrm.ldh + b * BLOCK_K)[c] = v;
+        }
+        act_store_quad<HP>(v, out, m, valid ? b : 0, c, valid);
     }
 }
 
