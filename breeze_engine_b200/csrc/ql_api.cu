@@ -978,14 +978,35 @@ static int output_chunks(int M, int N) {
     return std::max(1, chunks);
 }
 
+// A decode-size call whose A is pinned host memory that this device can read
+// (and 16-byte aligned) skips the host -> device copy: the quantizer reads A
+// over the bus itself, once, which removes one copy operation from the call's
+// critical path.  nullptr: copy A in as usual.
+static const float* direct_host_view(const float* A) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, A) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (attr.type != cudaMemoryTypeHost || !attr.devicePointer) return nullptr;
+    if (reinterpret_cast<uintptr_t>(attr.devicePointer) % 16) return nullptr;
+    return static_cast<const float*>(attr.devicePointer);
+}
+
 // Enqueues one host-pointer call on s (and the copy stream, joined back into
 // s): copy A in, quantize and multiply (in output column chunks whose copies
 // overlap the next chunk), copy C and the device error word out.  Nothing
 // here synchronises; the caller drains both streams.
 static int enqueue_host_call(const Weight* w, const float* A, int M, float* C, DeviceState* st, cudaStream_t s,
                              bool hp, float* dA, float* dC, void* ws, size_t ws_bytes, int* err_word) {
-    cudaError_t e = cudaMemcpyAsync(dA, A, static_cast<size_t>(M) * w->K * 4, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_status(e);
+    cudaError_t e = cudaSuccess;
+    const float* direct = use_gemm(M) ? nullptr : direct_host_view(A);
+    if (direct) {
+        dA = const_cast<float*>(direct);           // read by the quantizer only
+    } else {
+        e = cudaMemcpyAsync(dA, A, static_cast<size_t>(M) * w->K * 4, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
     const int chunks = output_chunks(M, w->N);
     if (chunks == 1) {
         int rc = run_matmul(w, dA, M, dC, nullptr, ws, ws_bytes, s, hp);

@@ -80,3 +80,36 @@ def test_repacked_weight_behind_the_same_buffers():
         assert not np.array_equal(outs[0], outs[1])
     finally:
         qlc.set_hi_prec(False)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_pinned_input_aligned_or_not(bits, oracle):
+    """A pinned, 16-byte aligned A is read by the quantizer directly (no copy
+    in); one that starts 4 bytes into its allocation is copied in as usual;
+    pageable A is copied in.  Same bits every way."""
+    import torch
+    lib = L.load()
+    M, N, K = 3, 4096, 512
+    qw, sc, h = _pack(N, K, bits, 11)
+    buf = torch.empty(M * K + 8, dtype=torch.float32).pin_memory()
+    c = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    rng = np.random.default_rng(5)
+    qlc.set_hi_prec(True)
+    try:
+        for off in (0, 1, 4, None):
+            x = rng.standard_normal((M, K)).astype(np.float32)
+            if off is None:
+                a_ptr, keep = x.ctypes.data, x                       # pageable
+            else:
+                a = buf[off:off + M * K].view(M, K)
+                a.copy_(torch.from_numpy(x))
+                a_ptr, keep = a.data_ptr(), a
+            c.fill_(-1.0)
+            lib.i4_matmul(ctypes.c_void_p(h), ctypes.c_void_p(a_ptr), M, ctypes.c_void_p(c.data_ptr()))
+            assert lib.ql_last_status() == 0, off
+            want = oracle.matmul(qw, sc, None, N, K, bits, x, hi_prec=True)
+            assert np.array_equal(c.numpy().view(np.uint32), want.view(np.uint32)), off
+            del keep
+    finally:
+        qlc.free(h)
+        qlc.set_hi_prec(False)
