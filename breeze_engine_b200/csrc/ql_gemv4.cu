@@ -54,6 +54,7 @@ struct Dp4aParams {
     int M, N, nblk, G, ldc;
     int TPB, TPBA, QREC;
     int Q4, SPLIT, BPS, STAGES;   // row-group quads per CTA, K split, blocks per stage, ring depth
+    int PROD;                     // producer warps (producer p issues the stages p, p + PROD, ...)
     uint32_t stage_bytes, off_Q, off_relay, off_stages;
 };
 
@@ -138,7 +139,7 @@ __device__ __forceinline__ void d4_record(const uint8_t* rec, const uint8_t* qre
 }  // namespace
 
 template <bool HALF, bool ZP, int MTOK, bool HP, bool OUT_CS>
-__global__ void __launch_bounds__(288) decode_dp4a_kernel(const Dp4aParams p) {
+__global__ void __launch_bounds__(384) decode_dp4a_kernel(const Dp4aParams p) {
     constexpr int TB = 256, SB = HALF ? 32 : 64, ZB = ZP ? 16 : 0, REC = TB + SB + ZB;
     constexpr int LB = HP ? 16 : 8;                 // activation bytes per fragment slot
     extern __shared__ __align__(128) uint8_t smem[];
@@ -166,9 +167,12 @@ __global__ void __launch_bounds__(288) decode_dp4a_kernel(const Dp4aParams p) {
     __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == consumers) {
-        // ------------------------------------------------------------ producer
+    if (warp >= consumers) {
+        // ----------------------------------------------------------- producers
+        // producer pr issues the stages i = pr (mod PROD); STAGES is a multiple
+        // of PROD, so it waits only on ring slots it filled itself
         if (lane != 0) return;
+        const int pr = warp - consumers;
         auto issue = [&](int i, bool weights, bool acts) {
             const int s = i % p.STAGES;
             const uint32_t base = smem_u32(stages + static_cast<size_t>(s) * p.stage_bytes);
@@ -185,14 +189,14 @@ __global__ void __launch_bounds__(288) decode_dp4a_kernel(const Dp4aParams p) {
             if (acts) bulk_g2s(base + p.off_Q, p.q + static_cast<size_t>(b0) * p.QREC, nb * p.QREC, full);
         };
         const int first = min(p.STAGES, nst);
-        for (int i = 0; i < first; ++i) issue(i, true, false);
+        for (int i = pr; i < first; i += p.PROD) issue(i, true, false);
         pdl_wait();                                   // activations come from the previous grid
-        for (int i = 0; i < first; ++i) issue(i, false, true);
-        for (int i = first; i < nst; ++i) {
+        for (int i = pr; i < first; i += p.PROD) issue(i, false, true);
+        for (int i = first + ((pr - first) % p.PROD + p.PROD) % p.PROD; i < nst; i += p.PROD) {
             const int s = i % p.STAGES;
             if (!mbar_wait(smem_u32(&empty_bar[s]), ((i / p.STAGES) - 1) & 1, p.err)) {
-                for (int j = max(0, i - p.STAGES); j < i; ++j)      // let issued copies land
-                    if (!mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
+                for (int j = i - p.STAGES; j < i; j += p.PROD)       // let this producer's copies land
+                    if (j >= 0 && !mbar_wait(smem_u32(&full_bar[j % p.STAGES]), (j / p.STAGES) & 1, p.err)) break;
                 return;
             }
             issue(i, true, true);
@@ -527,7 +531,7 @@ int* device_error_word();   // ql_api.cu
 namespace {
 
 struct D4Config {
-    int Q4, SPLIT, BPS, STAGES;
+    int Q4, SPLIT, BPS, STAGES, PROD;
 };
 
 int d4_sms() {
@@ -552,7 +556,7 @@ int d4_stage_bytes(int R, int BPS, int rec, int qrec) { return (R * BPS * rec + 
 // stages below that (13 us for 17408 x 5120).  Deeper stages (16 blocks),
 // two-warp splits and 8-warp splits each measured slower.  Layers that give
 // fewer than 128 quads take the chain variant (use_chain).
-D4Config d4_plan(int G, int nblk, int rec, int qrec) {
+D4Config d4_plan(int G, int nblk, int rec, int qrec, int mtok) {
     const int sms = d4_sms();
     const long long quads = (G + 3) / 4;
     D4Config c;
@@ -560,20 +564,27 @@ D4Config d4_plan(int G, int nblk, int rec, int qrec) {
     c.SPLIT = 4;
     c.BPS = D4_C;
     c.STAGES = quads >= 3LL * sms ? 4 : 8;
+    // Two producer warps at one token, or when few quads share an SM (one
+    // issuing thread's copies stream at most ~16-19 GB/s); measured on B200:
+    // 17408 x 5120 14.6 -> 11.9 us (M = 1) and 16.2 -> 14.7 us (M = 2),
+    // 34816 x 5120 20.9 -> 19.5 us and 151936 x 4096 66.5 -> 61.1 us at M = 1,
+    // but 90 -> 101 us for 151936 x 4096 at M = 2; four producers were no better.
+    c.PROD = (mtok == 1 || quads < 3LL * sms) ? 2 : 1;
     while (c.SPLIT > 1 && (nblk + c.BPS - 1) / c.BPS < 2 * c.SPLIT) c.SPLIT /= 2;
     if (c.STAGES % c.SPLIT) c.STAGES = ((c.STAGES + c.SPLIT - 1) / c.SPLIT) * c.SPLIT;
     if (c.STAGES < 2) c.STAGES = 2;
     (void)rec;
     (void)qrec;
-    // Tuning override "Q4,SPLIT,BPS,STAGES" (0 keeps the planner's value); the
-    // launch checks reject values that break the kernel's invariants.
+    // Tuning override "Q4,SPLIT,BPS,STAGES[,PROD]" (0 keeps the planner's
+    // value); the launch checks reject values that break the kernel's invariants.
     if (const char* env = std::getenv("BREEZE_QL_DP4A_CONFIG")) {
-        int q = 0, sp = 0, b = 0, st = 0;
-        if (std::sscanf(env, "%d,%d,%d,%d", &q, &sp, &b, &st) == 4) {
+        int q = 0, sp = 0, b = 0, st = 0, pd = 0;
+        if (std::sscanf(env, "%d,%d,%d,%d,%d", &q, &sp, &b, &st, &pd) >= 4) {
             if (q > 0) c.Q4 = q;
             if (sp > 0) c.SPLIT = sp;
             if (b > 0) c.BPS = b;
             if (st > 0) c.STAGES = st;
+            if (pd > 0) c.PROD = pd;
         }
     }
     return c;
@@ -583,11 +594,12 @@ template <bool HALF, bool ZP, int MTOK, bool HP, bool OUT_CS>
 cudaError_t d4_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     constexpr int REC = 256 + (HALF ? 32 : 64) + (ZP ? 16 : 0);
     Dp4aParams p = p0;
-    const D4Config c = d4_plan(p.G, p.nblk, REC, p.QREC);
+    const D4Config c = d4_plan(p.G, p.nblk, REC, p.QREC, MTOK);
     p.Q4 = c.Q4;
     p.SPLIT = c.SPLIT;
     p.BPS = c.BPS;
     p.STAGES = c.STAGES;
+    p.PROD = c.PROD;
     const int R = 4 * c.Q4;
     p.off_Q = R * c.BPS * REC;
     p.stage_bytes = d4_stage_bytes(R, c.BPS, REC, p.QREC);
@@ -600,7 +612,8 @@ cudaError_t d4_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     const int consumers = c.Q4 * c.SPLIT;
     // the carve-up must fit the SM and keep the invariants the kernel relies on
     if (smem > 227 * 1024 || c.BPS < 1 || c.STAGES < 2 || c.Q4 < 1 || c.Q4 > 2 || c.SPLIT < 1 || c.SPLIT > 8 ||
-        consumers > 8 || (c.STAGES % c.SPLIT) || (p.QREC % 16) || (REC % 16) || (p.off_Q % 16))
+        consumers > 8 || (c.STAGES % c.SPLIT) || c.PROD < 1 || c.PROD > 4 || (c.STAGES % c.PROD) ||
+        (p.QREC % 16) || (REC % 16) || (p.off_Q % 16))
         return cudaErrorInvalidConfiguration;
     auto kern = decode_dp4a_kernel<HALF, ZP, MTOK, HP, OUT_CS>;
     static int configured[64] = {0};
@@ -614,7 +627,7 @@ cudaError_t d4_launch(const Dp4aParams& p0, cudaStream_t stream, bool pdl) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.G + R - 1) / R);
-    cfg.blockDim = dim3(32 * (consumers + 1));
+    cfg.blockDim = dim3(32 * (consumers + c.PROD));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

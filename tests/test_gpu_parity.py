@@ -404,3 +404,26 @@ def test_decode_kernel_producers(bits, half, cfg, oracle, monkeypatch):
     finally:
         qlc.free(h)
         qlc.set_hi_prec(False)
+
+
+@pytest.mark.parametrize("cfg", ["0,0,0,0,2", "0,0,0,0,4", "1,2,8,4,2", "2,4,8,8,4", "1,4,16,4,4", "1,1,5,2,2"])
+@pytest.mark.parametrize("N", [8208, 1008])
+def test_dp4a_relay_producers(cfg, N, oracle, monkeypatch):
+    """The relay variant of the dp4a decode kernel with one to four producer
+    warps (each issuing every PROD-th stage) gives the same bits at one and two
+    tokens: a wide layer (a partial last quad) and, forced with
+    BREEZE_QL_DP4A_KERNEL=relay, a small one; 89 blocks, so stages end
+    partial."""
+    K = 2848
+    qw, sc, qz = _weights(N, K, 4, True, True, 13)
+    h = qlc.prepack(qw, sc, qz, N, K, 4)
+    qlc.set_hi_prec(True)
+    monkeypatch.setenv("BREEZE_QL_DP4A_KERNEL", "relay")
+    monkeypatch.setenv("BREEZE_QL_DP4A_CONFIG", cfg)
+    try:
+        for M in (1, 2):
+            a = np.random.default_rng(M + 3).standard_normal((M, K)).astype(np.float32)
+            assert bits_equal(qlc.matmul_dev(h, a, N), oracle.matmul(qw, sc, qz, N, K, 4, a, hi_prec=True)), M
+    finally:
+        qlc.free(h)
+        qlc.set_hi_prec(False)
