@@ -84,7 +84,11 @@ void i4_free(void* handle);
 /* Replaces i4_matmul (kernel/quantized_matmul.cpp:526-552): C[M,N] =
  * A[M,K] @ dequant(W).T with host fp32 row-major A and C, synchronous.  Like
  * the reference it returns nothing; a failure leaves C untouched and sets
- * ql_last_status(). */
+ * ql_last_status(), which also reports QL_ETIMEOUT when a bounded device wait
+ * of the call gave up.  Page-locked (pinned) host buffers are fastest: at
+ * decode sizes (M <= 64) a pinned, 16-byte aligned A is read by the quantizer
+ * directly instead of being copied in, and outputs of 2 MB or more are copied
+ * back in column chunks that overlap the matmul; pageable buffers work too. */
 void i4_matmul(void* handle, const float* A, int M, float* C);
 
 /* Replaces i4_matmul_region (kernel/quantized_matmul.cpp:554-572): the same
